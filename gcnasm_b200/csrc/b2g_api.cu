@@ -1,0 +1,722 @@
+// b2g_api.cu -- C ABI of the B200 FP8 GEMM library (declared in include/b2g/gemm.h).
+//
+// Host responsibilities: argument validation (status codes, never exit), tile
+// selection (the reference's select_kernel algorithm over this library's own
+// tile manifest), TMA tensor-map encoding, split-K bookkeeping, per-device
+// scratch (split-K workspace, per-call scale re-layout) and the device status
+// word the kernels' bounded waits report into.
+#include "b2g/gemm.h"
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "b2g_aux.cuh"
+#include "b2g_gemm.cuh"
+
+using namespace b2g;
+
+namespace {
+
+constexpr int kVersion = 100;  // 0.1.0
+
+thread_local char g_last_error[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+#define B2G_CUDA(call)                                                                  \
+  do {                                                                                  \
+    cudaError_t e_ = (call);                                                            \
+    if (e_ != cudaSuccess)                                                              \
+      return fail(B2G_ERR_CUDA, "%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), \
+                  __FILE__, __LINE__);                                                  \
+  } while (0)
+
+std::atomic<unsigned long long> g_timeout_ns{4000ull * 1000000ull};
+std::atomic<int> g_force_stall{0};
+
+// ------------------------------------------------------------------ driver entry
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// ------------------------------------------------------------------ per-device state
+struct DevState {
+  bool init = false;
+  int sms = 0;
+  int* status = nullptr;  // device status word written by bounded waits
+  void* ws = nullptr;     // scratch: split-K workspace and per-call scale re-layout
+  size_t ws_bytes = 0;
+  std::vector<const void*> configured;  // kernels whose smem attribute is set
+};
+
+std::mutex g_mu;
+DevState g_dev[64];
+
+int device_state(DevState** out, int* dev_out = nullptr) {
+  int dev = 0;
+  B2G_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(B2G_ERR_NO_DEVICE, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_mu);
+  DevState& d = g_dev[dev];
+  if (!d.init) {
+    int major = 0;
+    B2G_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+    if (major != 10) return fail(B2G_ERR_NO_DEVICE, "device %d is sm_%d0; this library targets sm_100a", dev, major);
+    B2G_CUDA(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev));
+    B2G_CUDA(cudaMalloc(&d.status, sizeof(int)));
+    B2G_CUDA(cudaMemset(d.status, 0, sizeof(int)));
+    d.init = true;
+  }
+  *out = &d;
+  if (dev_out) *dev_out = dev;
+  return B2G_OK;
+}
+
+// Grow-only per-device scratch.  Growing frees the old block with cudaFree,
+// which waits for outstanding device work, so no kernel still reads it.
+int workspace(DevState* d, size_t bytes, void** out) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (d->ws_bytes < bytes) {
+    if (d->ws) B2G_CUDA(cudaFree(d->ws));
+    d->ws = nullptr;
+    d->ws_bytes = 0;
+    size_t want = std::max(bytes, size_t(1) << 20);
+    if (cudaMalloc(&d->ws, want) != cudaSuccess) {
+      (void)cudaGetLastError();
+      return fail(B2G_ERR_WORKSPACE, "could not allocate %zu bytes of scratch", want);
+    }
+    d->ws_bytes = want;
+  }
+  *out = d->ws;
+  return B2G_OK;
+}
+
+int ensure_smem_attr(DevState* d, const void* fn, int bytes) {
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (std::find(d->configured.begin(), d->configured.end(), fn) != d->configured.end()) return B2G_OK;
+  }
+  B2G_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  std::lock_guard<std::mutex> lk(g_mu);
+  d->configured.push_back(fn);
+  return B2G_OK;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline int cdiv(long long a, long long b) { return static_cast<int>((a + b - 1) / b); }
+inline int grid_for(long long work, int per_block, int sms) {
+  long long g = (work + per_block - 1) / per_block;
+  return static_cast<int>(std::max<long long>(1, std::min<long long>(g, 8LL * sms)));
+}
+
+// ------------------------------------------------------------------ tile manifest
+struct TileCfg {
+  int tile_m, tile_n, splitk, bpre;
+  const char* name;
+};
+// Same columns as the reference manifest f4gemm_bf16_per1x32Fp4.csv
+// (tile_M, tile_N, splitK, bpreshuffle, knl_name), one row per kernel variant.
+const TileCfg kManifest[] = {
+    {128, 256, 1, 0, "b2g_sm100a_fp8_128x256"},
+    {128, 128, 1, 0, "b2g_sm100a_fp8_128x128"},
+    {128, 256, 1, 1, "b2g_sm100a_fp8_128x256_bpreshuffle"},
+    {128, 128, 1, 1, "b2g_sm100a_fp8_128x128_bpreshuffle"},
+};
+constexpr int kManifestN = sizeof(kManifest) / sizeof(kManifest[0]);
+
+// The reference heuristic (asm_f4gemm/f4gemm.hpp:210-267): fewest waves of
+// ceil(tiles * splitK / num_sm); ties go to fewer idle SMs, then to the larger
+// tile_m*tile_n/(tile_m+tile_n); manifest order breaks remaining ties.
+void select_tile(int M, int N, int num_sm, int log2_k_split, int bpreshuffle, int* idx, int* log2_out,
+                 int max_tile_n = 1 << 30) {
+  uint32_t empty_cu = static_cast<uint32_t>(num_sm);
+  uint32_t round = 0xffffffffu;
+  float effi = 1.0f;
+  const int split_en = log2_k_split > 0 ? 1 : 0;
+  const int bpre_en = bpreshuffle ? 1 : 0;
+  int sel = -1, sel_split = 1;
+  for (int i = 0; i < kManifestN; ++i) {
+    const TileCfg& c = kManifest[i];
+    if (c.bpre != bpre_en || c.splitk < split_en || c.tile_n > max_tile_n) continue;
+    if (c.tile_m == 128 && c.tile_n == 512 && (N % c.tile_n) != 0) continue;
+    int cand[4], nc = 0;
+    if (log2_k_split >= 0 && c.splitk) cand[nc++] = 1 << log2_k_split;
+    else if (c.splitk) { cand[0] = 2; cand[1] = 4; cand[2] = 8; cand[3] = 16; nc = 4; }
+    else cand[nc++] = 1;
+    for (int j = 0; j < nc; ++j) {
+      const int sk = cand[j];
+      const uint32_t tg = static_cast<uint32_t>(((M + c.tile_m - 1) / c.tile_m) * ((N + c.tile_n - 1) / c.tile_n) * sk);
+      const uint32_t lr = (tg + num_sm - 1) / num_sm;
+      const float le = static_cast<float>(c.tile_m) * c.tile_n / (c.tile_m + c.tile_n);
+      const bool earlier = lr < round, same = lr == round;
+      const bool more_busy = empty_cu > (lr * static_cast<uint32_t>(num_sm) - tg);
+      const bool better = le > effi;
+      if (earlier || (same && (more_busy || better))) {
+        round = lr;
+        empty_cu = lr * static_cast<uint32_t>(num_sm) - tg;
+        effi = le;
+        sel = i;
+        sel_split = sk;
+      }
+    }
+  }
+  int l = 0;
+  while (sel_split >>= 1) ++l;
+  *idx = sel;
+  *log2_out = l;
+}
+
+// ------------------------------------------------------------------ tensor maps
+int encode(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base, const cuuint64_t* dims,
+           const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle sw) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(B2G_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint32_t es[5] = {1, 1, 1, 1, 1};
+  CUresult r = fn(m, dt, rank, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(B2G_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled rejected a %d-D map (error %d)", rank, (int)r);
+  return B2G_OK;
+}
+
+// ------------------------------------------------------------------ generic launch
+struct Req {
+  int mode = kModePlain;
+  int bn = 0;  // 0: heuristic
+  bool bpre = false;
+  bool out_f32 = false;
+  int M = 0, N = 0, K = 0, batch = 1;
+  const void* a = nullptr;
+  long long lda = 0, a_bstride = 0;  // bytes
+  const void* b = nullptr;
+  long long ldb = 0, b_bstride = 0;  // bytes
+  void* c = nullptr;
+  long long ldc = 0, c_bstride = 0;  // elements
+  float alpha = 1.f;
+  const uint8_t* sfa = nullptr;
+  const uint8_t* sfb = nullptr;
+  long long sfa_bstride = 0, sfb_bstride = 0;
+  const float* bsa = nullptr;
+  const float* bsb = nullptr;
+  long long stride_sfa = 0, stride_sfb = 0, bsa_bstride = 0, bsb_bstride = 0;
+  int group_n = 128;
+  int log2_k_split = 0;
+  size_t ws_offset = 0;  // scratch bytes already claimed by the caller of run_gemm
+  cudaStream_t stream = nullptr;
+};
+
+template <class Cfg>
+int launch_cfg(DevState* d, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid,
+               cudaStream_t st) {
+  const void* fn = reinterpret_cast<const void*>(&b2g_gemm_kernel<Cfg>);
+  int rc = ensure_smem_attr(d, fn, Cfg::kSmemBytes);
+  if (rc) return rc;
+  b2g_gemm_kernel<Cfg><<<grid, Cfg::kThreads, Cfg::kSmemBytes, st>>>(ta, tb, p);
+  B2G_CUDA(cudaGetLastError());
+  return B2G_OK;
+}
+
+template <int kMode, int kBN>
+int dispatch_pre_out(DevState* d, bool pre, bool f32, const CUtensorMap& ta, const CUtensorMap& tb,
+                     const GemmParams& p, int grid, cudaStream_t st) {
+  if (kMode == kModeBlk) {  // blockwise path: row-major B only
+    return f32 ? launch_cfg<GemmCfg<kMode, kBN, false, true>>(d, ta, tb, p, grid, st)
+               : launch_cfg<GemmCfg<kMode, kBN, false, false>>(d, ta, tb, p, grid, st);
+  } else {
+    if (pre)
+      return f32 ? launch_cfg<GemmCfg<kMode, kBN, true, true>>(d, ta, tb, p, grid, st)
+                 : launch_cfg<GemmCfg<kMode, kBN, true, false>>(d, ta, tb, p, grid, st);
+    return f32 ? launch_cfg<GemmCfg<kMode, kBN, false, true>>(d, ta, tb, p, grid, st)
+               : launch_cfg<GemmCfg<kMode, kBN, false, false>>(d, ta, tb, p, grid, st);
+  }
+}
+
+template <int kMode>
+int dispatch_bn(DevState* d, int bn, bool pre, bool f32, const CUtensorMap& ta, const CUtensorMap& tb,
+                const GemmParams& p, int grid, cudaStream_t st) {
+  // The blockwise mode keeps 128 fp32 sums per epilogue thread at kBN = 256,
+  // more than the 168-register budget of a 10-warp CTA; it runs 128-wide tiles.
+  if (kMode != kModeBlk && bn == 256) return dispatch_pre_out<kMode, 256>(d, pre, f32, ta, tb, p, grid, st);
+  return dispatch_pre_out<kMode, 128>(d, pre, f32, ta, tb, p, grid, st);
+}
+
+int maybe_sync_check() {
+  static const bool on = [] {
+    const char* e = getenv("B2G_SYNC_CHECK");
+    return e && e[0] == '1';
+  }();
+  if (!on) return B2G_OK;
+  int st = 0;
+  int rc = b2g_device_status(&st, 1);
+  if (rc) return rc;
+  if (st) return fail(B2G_ERR_DEVICE_TIMEOUT, "kernel reported device status %d", st);
+  return B2G_OK;
+}
+
+int run_gemm(const Req& r) {
+  int rc = B2G_OK;
+  if (r.M <= 0 || r.N <= 0 || r.K <= 0 || r.batch <= 0) return fail(B2G_ERR_INVALID_ARG, "non-positive problem size");
+  if (!r.a || !r.b || !r.c) return fail(B2G_ERR_INVALID_ARG, "null A/B/C pointer");
+  if (r.N % 16) return fail(B2G_ERR_UNSUPPORTED, "N (%d) must be a multiple of 16", r.N);
+  if (r.K % 16) return fail(B2G_ERR_UNSUPPORTED, "K (%d) must be a multiple of 16", r.K);
+  if (r.mode == kModeMX && r.K % 32) return fail(B2G_ERR_UNSUPPORTED, "MXFP8 needs K %% 32 == 0 (K=%d)", r.K);
+  if (r.mode == kModeBlk && r.K % 128) return fail(B2G_ERR_UNSUPPORTED, "block-scale GEMM needs K %% 128 == 0 (K=%d)", r.K);
+  if (!aligned16(r.a) || !aligned16(r.b) || !aligned16(r.c)) return fail(B2G_ERR_ALIGNMENT, "A/B/C must be 16-byte aligned");
+  if (r.lda < r.K || r.lda % 16) return fail(B2G_ERR_ALIGNMENT, "A row stride %lld must be >= K and a multiple of 16", r.lda);
+  if (!r.bpre && (r.ldb < r.K || r.ldb % 16)) return fail(B2G_ERR_ALIGNMENT, "B row stride %lld must be >= K and a multiple of 16", r.ldb);
+  if (r.bpre && r.K % 32) return fail(B2G_ERR_UNSUPPORTED, "preshuffled B needs K %% 32 == 0");
+  const int esz = r.out_f32 ? 4 : 2;
+  if (r.ldc < r.N || (r.ldc * esz) % 16) return fail(B2G_ERR_ALIGNMENT, "C row stride %lld must be >= N and 16-byte aligned", r.ldc);
+  if (r.batch > 1 && (r.a_bstride % 16 || r.b_bstride % 16 || (r.c_bstride * esz) % 16))
+    return fail(B2G_ERR_ALIGNMENT, "batch strides must be 16-byte multiples");
+  if (r.mode == kModeMX) {
+    if (!r.sfa || !r.sfb) return fail(B2G_ERR_INVALID_ARG, "null scale pointer");
+    if (!aligned16(r.sfa) || !aligned16(r.sfb) || r.sfa_bstride % 16 || r.sfb_bstride % 16)
+      return fail(B2G_ERR_ALIGNMENT, "scale buffers must be 16-byte aligned");
+  }
+  if (r.mode == kModeBlk) {
+    if (!r.bsa || !r.bsb) return fail(B2G_ERR_INVALID_ARG, "null scale pointer");
+    if (r.group_n != 1 && r.group_n != 128) return fail(B2G_ERR_INVALID_ARG, "group_n must be 1 or 128");
+    if (r.N % r.group_n) return fail(B2G_ERR_UNSUPPORTED, "N %% GROUP_N != 0");
+    if (r.stride_sfa < r.M) return fail(B2G_ERR_INVALID_ARG, "stride_sfa < M");
+    if (r.group_n == 1 && (r.stride_sfb < r.N || r.stride_sfb % 4 || !aligned16(r.bsb) || r.bsb_bstride % 4))
+      return fail(B2G_ERR_ALIGNMENT, "GROUP_N=1 SFB needs stride_sfb >= N, a multiple of 4, and a 16-byte aligned base");
+    if (r.group_n == 128 && r.stride_sfb < r.K / 128) return fail(B2G_ERR_INVALID_ARG, "stride_sfb < K/128");
+  }
+
+  DevState* d = nullptr;
+  rc = device_state(&d);
+  if (rc) return rc;
+
+  // ---- tile + split
+  int bn = r.bn, l2 = r.log2_k_split;
+  if (r.mode == kModeBlk && bn == 256) bn = 128;
+  if (bn == 0) {
+    int idx = -1, lsel = 0;
+    select_tile(r.M, r.N, d->sms, r.log2_k_split, r.bpre ? 1 : 0, &idx, &lsel, r.mode == kModeBlk ? 128 : 1 << 30);
+    if (idx < 0) return fail(B2G_ERR_UNSUPPORTED, "no tile in the manifest fits");
+    bn = kManifest[idx].tile_n;
+    l2 = lsel;
+  }
+  if (l2 < 0) l2 = 0;
+  if (l2 > 8) return fail(B2G_ERR_INVALID_ARG, "log2_k_split %d too large", l2);
+  const int KB = cdiv(r.K, 128);
+  int S = std::min(1 << l2, KB);
+  const int kb_per = cdiv(KB, S);
+  S = cdiv(KB, kb_per);
+
+  GemmParams p;
+  memset(&p, 0, sizeof(p));
+  p.M = r.M; p.N = r.N; p.K = r.K; p.batch = r.batch;
+  p.c = r.c; p.ldc = r.ldc; p.c_bstride = r.c_bstride;
+  p.alpha = r.alpha;
+  p.sfa = r.sfa; p.sfb = r.sfb;
+  p.sfa_rb = static_cast<long long>(cdiv(r.K, 128)) * 512;
+  p.sfb_rb = p.sfa_rb;
+  p.sfa_bstride = r.sfa_bstride; p.sfb_bstride = r.sfb_bstride;
+  p.sfb_blocks = cdiv(r.N, 128);
+  p.bsa = r.bsa; p.bsb = r.bsb;
+  p.stride_sfa = r.stride_sfa; p.stride_sfb = r.stride_sfb;
+  p.bsa_bstride = r.bsa_bstride; p.bsb_bstride = r.bsb_bstride;
+  p.group_n = r.group_n;
+  p.MT = cdiv(r.M, 128); p.NT = cdiv(r.N, bn);
+  p.S = S; p.KB = KB; p.kb_per_split = kb_per;
+  p.group_m = 8;
+  const long long units = static_cast<long long>(r.batch) * p.MT * p.NT * S;
+  if (units > 0x7fffffffLL) return fail(B2G_ERR_UNSUPPORTED, "problem too large");
+  p.num_units = static_cast<int>(units);
+  p.status = d->status;
+  p.timeout_ns = g_timeout_ns.load();
+  p.debug_stall = g_force_stall.load();
+
+  if (S == 1) p.out_mode = kOutStore;
+  else if (r.out_f32) p.out_mode = kOutAtomic;
+  else p.out_mode = kOutWorkspace;
+
+  // ---- tensor maps
+  CUtensorMap ta, tb;
+  {
+    cuuint64_t dims[3] = {(cuuint64_t)r.K, (cuuint64_t)r.M, (cuuint64_t)r.batch};
+    cuuint64_t str[2] = {(cuuint64_t)r.lda, (cuuint64_t)(r.batch > 1 ? r.a_bstride : r.lda * r.M)};
+    cuuint32_t box[3] = {128, 128, 1};
+    rc = encode(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, r.a, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  if (!r.bpre) {
+    cuuint64_t dims[3] = {(cuuint64_t)r.K, (cuuint64_t)r.N, (cuuint64_t)r.batch};
+    cuuint64_t str[2] = {(cuuint64_t)r.ldb, (cuuint64_t)(r.batch > 1 ? r.b_bstride : r.ldb * r.N)};
+    cuuint32_t box[3] = {128, (cuuint32_t)bn, 1};
+    rc = encode(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, r.b, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  } else {
+    // [N/16][K/16][16 rows][16 bytes] viewed as (k16, n16, n_grp, k_grp, batch) so
+    // that a box lands in smem as [k_grp][n][16 B]: the interleaved K-major
+    // operand layout of tcgen05.mma.
+    cuuint64_t dims[5] = {16, 16, (cuuint64_t)(r.N / 16), (cuuint64_t)(r.K / 16), (cuuint64_t)r.batch};
+    cuuint64_t str[4] = {16, (cuuint64_t)16 * r.K, 256,
+                         (cuuint64_t)(r.batch > 1 ? r.b_bstride : (long long)r.N * r.K)};
+    cuuint32_t box[5] = {16, 16, (cuuint32_t)(bn / 16), 8, 1};
+    rc = encode(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 5, r.b, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  }
+
+  // ---- split-K output preparation
+  if (p.out_mode == kOutAtomic) {
+    for (int bi = 0; bi < r.batch; ++bi)
+      B2G_CUDA(cudaMemset2DAsync(reinterpret_cast<float*>(r.c) + bi * r.c_bstride, r.ldc * 4, 0,
+                                 static_cast<size_t>(r.N) * 4, r.M, r.stream));
+  } else if (p.out_mode == kOutWorkspace) {
+    void* ws = nullptr;
+    const size_t need = r.ws_offset + static_cast<size_t>(S) * r.batch * r.M * r.N * 4;
+    rc = workspace(d, need, &ws);
+    if (rc) return rc;
+    p.ws = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + r.ws_offset);
+  }
+
+  const int grid = static_cast<int>(std::min<long long>(units, d->sms));
+  switch (r.mode) {
+    case kModePlain: rc = dispatch_bn<kModePlain>(d, bn, r.bpre, r.out_f32, ta, tb, p, grid, r.stream); break;
+    case kModeMX: rc = dispatch_bn<kModeMX>(d, bn, r.bpre, r.out_f32, ta, tb, p, grid, r.stream); break;
+    default: rc = dispatch_bn<kModeBlk>(d, bn, r.bpre, r.out_f32, ta, tb, p, grid, r.stream); break;
+  }
+  if (rc) return rc;
+
+  if (p.out_mode == kOutWorkspace) {
+    const long long work = static_cast<long long>(r.batch) * r.M * (r.N / 4);
+    const int g = grid_for(work, 256, d->sms);
+    if (r.out_f32)
+      b2g_splitk_reduce_kernel<true><<<g, 256, 0, r.stream>>>(p.ws, r.c, S, r.batch, r.M, r.N, r.ldc, r.c_bstride);
+    else
+      b2g_splitk_reduce_kernel<false><<<g, 256, 0, r.stream>>>(p.ws, r.c, S, r.batch, r.M, r.N, r.ldc, r.c_bstride);
+    B2G_CUDA(cudaGetLastError());
+  }
+  return maybe_sync_check();
+}
+
+}  // namespace
+
+// =================================================================== C ABI
+extern "C" {
+
+int b2g_version(void) { return kVersion; }
+const char* b2g_last_error(void) { return g_last_error; }
+
+const char* b2g_status_string(int s) {
+  switch (s) {
+    case B2G_OK: return "ok";
+    case B2G_ERR_INVALID_ARG: return "invalid argument";
+    case B2G_ERR_UNSUPPORTED: return "unsupported shape or layout";
+    case B2G_ERR_ALIGNMENT: return "misaligned pointer or stride";
+    case B2G_ERR_CUDA: return "CUDA error";
+    case B2G_ERR_DEVICE_TIMEOUT: return "device wait timed out";
+    case B2G_ERR_NO_DEVICE: return "no sm_100 device";
+    case B2G_ERR_WORKSPACE: return "scratch allocation failed";
+    default: return "unknown status";
+  }
+}
+
+int b2g_set_wait_timeout_ms(int ms) {
+  if (ms <= 0) return fail(B2G_ERR_INVALID_ARG, "timeout must be positive");
+  g_timeout_ns.store(static_cast<unsigned long long>(ms) * 1000000ull);
+  return B2G_OK;
+}
+
+int b2g_debug_force_stall(int on) {
+  g_force_stall.store(on ? 1 : 0);
+  return B2G_OK;
+}
+
+int b2g_device_status(int* status, int clear) {
+  if (!status) return fail(B2G_ERR_INVALID_ARG, "null status pointer");
+  DevState* d = nullptr;
+  int rc = device_state(&d);
+  if (rc) return rc;
+  B2G_CUDA(cudaDeviceSynchronize());
+  B2G_CUDA(cudaMemcpy(status, d->status, sizeof(int), cudaMemcpyDeviceToHost));
+  if (clear) B2G_CUDA(cudaMemset(d->status, 0, sizeof(int)));
+  return *status ? B2G_ERR_DEVICE_TIMEOUT : B2G_OK;
+}
+
+int b2g_manifest_size(void) { return kManifestN; }
+
+int b2g_manifest_entry(int i, int* tile_m, int* tile_n, int* splitk, int* bpreshuffle, const char** name) {
+  if (i < 0 || i >= kManifestN) return fail(B2G_ERR_INVALID_ARG, "manifest index %d out of range", i);
+  if (tile_m) *tile_m = kManifest[i].tile_m;
+  if (tile_n) *tile_n = kManifest[i].tile_n;
+  if (splitk) *splitk = kManifest[i].splitk;
+  if (bpreshuffle) *bpreshuffle = kManifest[i].bpre;
+  if (name) *name = kManifest[i].name;
+  return B2G_OK;
+}
+
+int b2g_select(int m, int n, int k, int num_sm, int log2_k_split, int bpreshuffle, int* index, int* tile_m,
+               int* tile_n, int* log2_split) {
+  (void)k;
+  if (m <= 0 || n <= 0 || num_sm <= 0) return fail(B2G_ERR_INVALID_ARG, "bad select arguments");
+  int idx = -1, l2 = 0;
+  select_tile(m, n, num_sm, log2_k_split, bpreshuffle, &idx, &l2);
+  if (index) *index = idx;
+  if (idx < 0) return fail(B2G_ERR_UNSUPPORTED, "no manifest entry fits");
+  if (tile_m) *tile_m = kManifest[idx].tile_m;
+  if (tile_n) *tile_n = kManifest[idx].tile_n;
+  if (log2_split) *log2_split = l2;
+  return B2G_OK;
+}
+
+int b2g_gemm_a8w8_blockscale(const opus_gemm_kargs* ka, int group_n, int out_dtype, int log2_k_split,
+                             void* stream) {
+  if (!ka) return fail(B2G_ERR_INVALID_ARG, "null kargs");
+  if (out_dtype != B2G_OUT_BF16 && out_dtype != B2G_OUT_F32) return fail(B2G_ERR_INVALID_ARG, "bad out_dtype");
+  Req r;
+  r.mode = kModeBlk;
+  r.out_f32 = out_dtype == B2G_OUT_F32;
+  r.M = ka->m; r.N = ka->n; r.K = ka->k; r.batch = ka->batch;
+  r.a = ka->ptr_a; r.lda = ka->stride_a; r.a_bstride = ka->stride_a_batch;
+  r.b = ka->ptr_b; r.ldb = ka->stride_b; r.b_bstride = ka->stride_b_batch;
+  r.c = ka->ptr_c; r.ldc = ka->stride_c; r.c_bstride = ka->stride_c_batch;
+  r.bsa = static_cast<const float*>(ka->ptr_sfa);
+  r.bsb = static_cast<const float*>(ka->ptr_sfb);
+  r.stride_sfa = ka->stride_sfa; r.stride_sfb = ka->stride_sfb;
+  r.bsa_bstride = ka->stride_sfa_batch; r.bsb_bstride = ka->stride_sfb_batch;
+  r.group_n = group_n;
+  r.log2_k_split = log2_k_split;
+  r.stream = static_cast<cudaStream_t>(stream);
+  return run_gemm(r);
+}
+
+static int a8w8_common(const opus_gemm_kargs_a8w8* ka, float alpha, int out_dtype, int log2_k_split, void* stream,
+                       bool pre) {
+  if (!ka) return fail(B2G_ERR_INVALID_ARG, "null kargs");
+  if (out_dtype != B2G_OUT_BF16 && out_dtype != B2G_OUT_F32) return fail(B2G_ERR_INVALID_ARG, "bad out_dtype");
+  Req r;
+  r.mode = kModePlain;
+  r.bpre = pre;
+  r.out_f32 = out_dtype == B2G_OUT_F32;
+  r.M = ka->m; r.N = ka->n; r.K = ka->k; r.batch = ka->batch;
+  r.a = ka->ptr_a; r.lda = ka->stride_a; r.a_bstride = ka->stride_a_batch;
+  r.b = ka->ptr_b; r.ldb = pre ? ka->k : ka->stride_b; r.b_bstride = ka->stride_b_batch;
+  r.c = ka->ptr_c; r.ldc = ka->stride_c; r.c_bstride = ka->stride_c_batch;
+  r.alpha = alpha;
+  r.log2_k_split = log2_k_split;
+  r.stream = static_cast<cudaStream_t>(stream);
+  return run_gemm(r);
+}
+
+int b2g_gemm_a8w8(const opus_gemm_kargs_a8w8* ka, float alpha, int out_dtype, int log2_k_split, void* stream) {
+  return a8w8_common(ka, alpha, out_dtype, log2_k_split, stream, false);
+}
+
+int b2g_gemm_a8w8_preshuffled(const opus_gemm_kargs_a8w8* ka, float alpha, int out_dtype, int log2_k_split,
+                              void* stream) {
+  return a8w8_common(ka, alpha, out_dtype, log2_k_split, stream, true);
+}
+
+long long b2g_sf_tc_bytes(int rows, int k) {
+  if (rows <= 0 || k <= 0) return 0;
+  return static_cast<long long>((rows + 127) / 128) * ((k / 32 + 3) / 4) * 512;
+}
+
+int b2g_gemm_mxfp8(const b2g_mxfp8_args* g, void* stream) {
+  if (!g) return fail(B2G_ERR_INVALID_ARG, "null args");
+  if (g->out_dtype != B2G_OUT_BF16 && g->out_dtype != B2G_OUT_F32) return fail(B2G_ERR_INVALID_ARG, "bad out_dtype");
+  Req r;
+  r.mode = kModeMX;
+  r.bpre = g->b_preshuffled != 0;
+  r.out_f32 = g->out_dtype == B2G_OUT_F32;
+  r.M = g->m; r.N = g->n; r.K = g->k;
+  r.a = g->a; r.lda = g->lda;
+  r.b = g->b; r.ldb = r.bpre ? g->k : g->ldb;
+  r.c = g->d; r.ldc = g->ldd;
+  r.alpha = g->alpha;
+  r.sfa = static_cast<const uint8_t*>(g->sfa);
+  r.sfb = static_cast<const uint8_t*>(g->sfb);
+  r.log2_k_split = g->log2_k_split;
+  r.stream = static_cast<cudaStream_t>(stream);
+  return run_gemm(r);
+}
+
+int b2g_gemm_mxfp8_f4gemm(const b2g_f4gemm_kargs* a, int bpreshuffle, int out_dtype, void* stream) {
+  if (!a) return fail(B2G_ERR_INVALID_ARG, "null kargs");
+  if (out_dtype != B2G_OUT_BF16 && out_dtype != B2G_OUT_F32) return fail(B2G_ERR_INVALID_ARG, "bad out_dtype");
+  if (a->beta != 0.0f) return fail(B2G_ERR_UNSUPPORTED, "beta != 0 (the C/bias path) is not supported");
+  const int M = static_cast<int>(a->M), N = static_cast<int>(a->N), K = static_cast<int>(a->K);
+  if (M <= 0 || N <= 0 || K <= 0) return fail(B2G_ERR_INVALID_ARG, "non-positive problem size");
+  if (K % 32) return fail(B2G_ERR_UNSUPPORTED, "K %% 32 != 0");
+  if (!a->ptr_ScaleA || !a->ptr_ScaleB || !a->ptr_A || !a->ptr_B || !a->ptr_D)
+    return fail(B2G_ERR_INVALID_ARG, "null pointer in kargs");
+  if (N % 16) return fail(B2G_ERR_UNSUPPORTED, "N (%d) must be a multiple of 16", N);
+  const int cols = K / 32;
+  const int snA = static_cast<int>(a->stride_ScaleA0), snB = static_cast<int>(a->stride_ScaleB0);
+  if (snA < cols || snA % 8 || snB < cols || snB % 8)
+    return fail(B2G_ERR_INVALID_ARG, "scale row strides must be the padded column count (>= K/32, multiple of 8)");
+  DevState* d = nullptr;
+  int rc = device_state(&d);
+  if (rc) return rc;
+  const long long tcA = b2g_sf_tc_bytes(M, K), tcB = b2g_sf_tc_bytes(N, K);
+  const size_t offB = static_cast<size_t>((tcA + 255) / 256 * 256);
+  const size_t offW = offB + static_cast<size_t>((tcB + 255) / 256 * 256);
+  void* ws = nullptr;
+  rc = workspace(d, offW, &ws);
+  if (rc) return rc;
+  uint8_t* sA = static_cast<uint8_t*>(ws);
+  uint8_t* sB = sA + offB;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  b2g_sf_f4gemm_to_tc_kernel<<<grid_for(tcA, 256, d->sms), 256, 0, st>>>(
+      static_cast<const uint8_t*>(a->ptr_ScaleA), M, cols, snA, sA);
+  b2g_sf_f4gemm_to_tc_kernel<<<grid_for(tcB, 256, d->sms), 256, 0, st>>>(
+      static_cast<const uint8_t*>(a->ptr_ScaleB), N, cols, snB, sB);
+  B2G_CUDA(cudaGetLastError());
+  Req r;
+  r.mode = kModeMX;
+  r.bpre = bpreshuffle != 0;
+  r.out_f32 = out_dtype == B2G_OUT_F32;
+  r.M = M; r.N = N; r.K = K;
+  r.a = a->ptr_A; r.lda = a->stride_A0;
+  r.b = a->ptr_B; r.ldb = r.bpre ? K : static_cast<long long>(a->stride_B0);
+  r.c = a->ptr_D; r.ldc = a->stride_C0;  // the reference kernels use stride_C0 for D
+  r.alpha = a->alpha;
+  r.sfa = sA; r.sfb = sB;
+  r.log2_k_split = a->log2_k_split;
+  r.ws_offset = offW;
+  r.stream = st;
+  return run_gemm(r);
+}
+
+// ------------------------------------------------------------ layout helpers
+int b2g_sf_rowmajor_to_tc(const void* src, int rows, int cols, long long ld, void* dst, void* stream) {
+  if (!src || !dst || rows <= 0 || cols <= 0 || ld < cols) return fail(B2G_ERR_INVALID_ARG, "bad arguments");
+  DevState* d = nullptr;
+  int rc = device_state(&d);
+  if (rc) return rc;
+  const long long total = static_cast<long long>((rows + 127) / 128) * ((cols + 3) / 4) * 512;
+  b2g_sf_rowmajor_to_tc_kernel<<<grid_for(total, 256, d->sms), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(src), rows, cols, ld, static_cast<uint8_t*>(dst));
+  B2G_CUDA(cudaGetLastError());
+  return B2G_OK;
+}
+
+int b2g_sf_f4gemm_to_tc(const void* src, int rows, int cols, int sn, void* dst, void* stream) {
+  if (!src || !dst || rows <= 0 || cols <= 0 || sn < cols || sn % 8) return fail(B2G_ERR_INVALID_ARG, "bad arguments");
+  DevState* d = nullptr;
+  int rc = device_state(&d);
+  if (rc) return rc;
+  const long long total = static_cast<long long>((rows + 127) / 128) * ((cols + 3) / 4) * 512;
+  b2g_sf_f4gemm_to_tc_kernel<<<grid_for(total, 256, d->sms), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(src), rows, cols, sn, static_cast<uint8_t*>(dst));
+  B2G_CUDA(cudaGetLastError());
+  return B2G_OK;
+}
+
+int b2g_shuffle_scale(const void* src, int rows, int cols, int sm, int sn, void* dst, void* stream) {
+  if (!src || !dst || rows <= 0 || cols <= 0 || sm < rows || sn < cols || sm % 32 || sn % 8)
+    return fail(B2G_ERR_INVALID_ARG, "bad arguments");
+  DevState* d = nullptr;
+  int rc = device_state(&d);
+  if (rc) return rc;
+  b2g_shuffle_scale_kernel<<<grid_for((long long)sm * sn, 256, d->sms), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(src), rows, cols, sm, sn, static_cast<uint8_t*>(dst));
+  B2G_CUDA(cudaGetLastError());
+  return B2G_OK;
+}
+
+static int shuffle_w(const void* src, void* dst, int n, int kp, void* stream, bool inverse) {
+  if (!src || !dst || n <= 0 || kp <= 0 || n % 16 || kp % 32) return fail(B2G_ERR_INVALID_ARG, "bad arguments");
+  if (!aligned16(src) || !aligned16(dst)) return fail(B2G_ERR_ALIGNMENT, "buffers must be 16-byte aligned");
+  DevState* d = nullptr;
+  int rc = device_state(&d);
+  if (rc) return rc;
+  const long long total = static_cast<long long>(n) * (kp / 16);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (inverse)
+    b2g_shuffle_weight_16x16_kernel<true><<<grid_for(total, 256, d->sms), 256, 0, st>>>(
+        static_cast<const uint4*>(src), static_cast<uint4*>(dst), n, kp / 16);
+  else
+    b2g_shuffle_weight_16x16_kernel<false><<<grid_for(total, 256, d->sms), 256, 0, st>>>(
+        static_cast<const uint4*>(src), static_cast<uint4*>(dst), n, kp / 16);
+  B2G_CUDA(cudaGetLastError());
+  return B2G_OK;
+}
+
+int b2g_shuffle_weight_16x16(const void* src, void* dst, int n, int kp, void* stream) {
+  return shuffle_w(src, dst, n, kp, stream, false);
+}
+int b2g_unshuffle_weight_16x16(const void* src, void* dst, int n, int kp, void* stream) {
+  return shuffle_w(src, dst, n, kp, stream, true);
+}
+
+// ------------------------------------------------------------ quantisers
+int b2g_quant_mxfp8(const float* x, int rows, int k, long long ldx, void* q, long long ldq, void* sf_tc,
+                    void* sf_rowmajor, void* stream) {
+  if (!x || !q || rows <= 0 || k <= 0 || k % 32 || ldx < k || ldq < k) return fail(B2G_ERR_INVALID_ARG, "bad arguments");
+  if (!aligned16(x) || ldx % 4 || ldq % 8 || (reinterpret_cast<uintptr_t>(q) & 7))
+    return fail(B2G_ERR_ALIGNMENT, "x must be 16-byte aligned with ldx %% 4 == 0; q 8-byte aligned with ldq %% 8 == 0");
+  DevState* d = nullptr;
+  int rc = device_state(&d);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (sf_tc) {  // padding of the atom layout holds 1.0
+    B2G_CUDA(cudaMemsetAsync(sf_tc, 0x7F, static_cast<size_t>(b2g_sf_tc_bytes(rows, k)), st));
+  }
+  const long long work = static_cast<long long>(rows) * (k / 8);
+  b2g_quant_mx_kernel<<<grid_for(work, 256, d->sms), 256, 0, st>>>(x, rows, k, ldx, static_cast<uint8_t*>(q), ldq,
+                                                                     static_cast<uint8_t*>(sf_tc),
+                                                                     static_cast<uint8_t*>(sf_rowmajor));
+  B2G_CUDA(cudaGetLastError());
+  return B2G_OK;
+}
+
+int b2g_quant_1x128(const float* x, int rows, int k, void* q, float* sf, void* stream) {
+  if (!x || !q || !sf || rows <= 0 || k <= 0 || k % 128) return fail(B2G_ERR_INVALID_ARG, "bad arguments");
+  if (!aligned16(x) || !aligned16(q)) return fail(B2G_ERR_ALIGNMENT, "x and q must be 16-byte aligned");
+  DevState* d = nullptr;
+  int rc = device_state(&d);
+  if (rc) return rc;
+  const long long warps = static_cast<long long>(rows) * (k / 128);
+  b2g_quant_1x128_kernel<<<grid_for(warps * 32, 256, d->sms), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, rows, k, static_cast<uint8_t*>(q), sf);
+  B2G_CUDA(cudaGetLastError());
+  return B2G_OK;
+}
+
+int b2g_quant_128x128(const float* x, int n, int k, void* q, float* sf, void* stream) {
+  if (!x || !q || !sf || n <= 0 || k <= 0 || n % 128 || k % 128) return fail(B2G_ERR_INVALID_ARG, "bad arguments");
+  if (!aligned16(x) || !aligned16(q)) return fail(B2G_ERR_ALIGNMENT, "x and q must be 16-byte aligned");
+  DevState* d = nullptr;
+  int rc = device_state(&d);
+  if (rc) return rc;
+  const int tiles = (n / 128) * (k / 128);
+  b2g_quant_128x128_kernel<<<std::min(tiles, 8 * d->sms), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, n, k, static_cast<uint8_t*>(q), sf);
+  B2G_CUDA(cudaGetLastError());
+  return B2G_OK;
+}
+
+}  // extern "C"

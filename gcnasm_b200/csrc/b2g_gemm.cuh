@@ -1,0 +1,428 @@
+// b2g_gemm.cuh -- persistent, warp-specialised FP8 GEMM for sm_100a.
+//
+//   C[b, m, n] = epilogue( sum_k A[b, m, k] * B[b, n, k] )      (TN: both K-major)
+//
+// One kernel template covers the reference's opus_gemm FP8 family:
+//   kModePlain : fp8_gemm (opus_gemm/fp8_gemm/gemm_a8w8_8wave.cc:261-563) plus a
+//                per-tensor alpha in the epilogue;
+//   kModeMX    : MXFP8, E4M3 with one UE8M0 scale per 1x32 K-block, applied by
+//                the tensor core (tcgen05.mma kind::mxf8f6f4.block_scale);
+//   kModeBlk   : fp32 block scales, one per 1x128 of A and per 128x128 (GROUP_N=128,
+//                opus_gemm/block_scale_gemm) or 1x128 of B (GROUP_N=1,
+//                opus_gemm/block_scale_1x128x1_gemm).  Each 128-K block's MMA
+//                result lands in its own TMEM buffer and the epilogue warps fold
+//                it into fp32 registers with sfa*sfb -- the scale_c_tile step of
+//                block_scale_gemm/gemm_a8w8_blockscale_kernel_template.hpp:23-39,
+//                applied to TMEM accumulator tiles.
+//
+// Structure (one CTA per SM, 320 threads):
+//   warp 0      TMA producer: A/B tiles (and MX scale atoms) -> smem ring
+//   warp 1      TMEM owner + single-thread tcgen05.mma issuer
+//   warps 2..9  epilogue: tcgen05.ld -> registers -> scale / convert -> global
+// Tiles are 128 x kBN x 128 (M x N x K).  Work units (batch, m-tile, n-tile,
+// k-split) are walked statically: CTA i takes units i, i + grid, ... in a
+// grouped raster so that concurrently running tiles share A rows in L2.
+// Split-K partial sums are either added with fp32 vector reductions into a
+// zeroed C (fp32 output) or written to an fp32 workspace that
+// b2g_splitk_reduce sums and casts (the workspace + reduce scheme of
+// opus_gemm_dist/opus_gemm_mem_gemm_a2a/include/gfx950/splitk_reduce_gfx950.cuh:68-259).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cstdint>
+
+#include "b2g_ptx.cuh"
+
+namespace b2g {
+
+enum Mode : int { kModePlain = 0, kModeMX = 1, kModeBlk = 2 };
+enum OutMode : int { kOutStore = 0, kOutAtomic = 1, kOutWorkspace = 2 };
+
+struct GemmParams {
+  int M, N, K, batch;
+  // output: C[b][m][n] at c + b*c_bstride + m*ldc + n (elements of the output type)
+  void* c;
+  long long ldc, c_bstride;
+  int out_mode;
+  float* ws;  // split-K workspace [S][batch][M][N] fp32 (out_mode == kOutWorkspace)
+  float alpha;
+  // MX: UE8M0 scales in the tensor-core atom layout (128 rows x 4 K-blocks per
+  // 512-byte atom, atoms [row_block][k_block]); *_rb = bytes between row blocks
+  const uint8_t* sfa;
+  long long sfa_rb, sfa_bstride;
+  const uint8_t* sfb;
+  long long sfb_rb, sfb_bstride;
+  int sfb_blocks;  // ceil(N / 128): number of valid B row blocks
+  // kModeBlk: fp32 scales (opus_gemm_kargs semantics)
+  const float* bsa;
+  long long stride_sfa, bsa_bstride;  // SFA[kg * stride_sfa + m]
+  const float* bsb;
+  long long stride_sfb, bsb_bstride;  // GROUP_N=128: SFB[(n/128)*stride_sfb + kg]; GROUP_N=1: SFB[kg*stride_sfb + n]
+  int group_n;
+  // static schedule
+  int MT, NT, S, KB, kb_per_split, group_m, num_units;
+  // diagnostics
+  int* status;
+  unsigned long long timeout_ns;
+  int debug_stall;  // test hook: the MMA issuer waits on a barrier nothing arrives on
+};
+
+struct Unit {
+  int b, mt, nt, ks, kb0, kb1;
+};
+
+__host__ __device__ __forceinline__ Unit decode_unit(int u, const GemmParams& p) {
+  Unit w;
+  w.ks = u % p.S;
+  const int t = u / p.S;
+  const int tiles = p.MT * p.NT;
+  w.b = t / tiles;
+  const int r = t - w.b * tiles;
+  const int gsz = p.group_m * p.NT;
+  const int g = r / gsz;
+  const int first_m = g * p.group_m;
+  const int gm = (p.MT - first_m) < p.group_m ? (p.MT - first_m) : p.group_m;
+  const int q = r - g * gsz;
+  w.mt = first_m + q % gm;
+  w.nt = q / gm;
+  w.kb0 = w.ks * p.kb_per_split;
+  w.kb1 = (w.kb0 + p.kb_per_split) < p.KB ? (w.kb0 + p.kb_per_split) : p.KB;
+  return w;
+}
+
+// compile-time configuration -------------------------------------------------
+template <int kMode_, int kBN_, bool kBPre_, bool kOutF32_>
+struct GemmCfg {
+  static constexpr int kMode = kMode_;
+  static constexpr int kBN = kBN_;
+  static constexpr bool kBPre = kBPre_;     // B given 16x16-preshuffled ([N/16][K/16][16][16] bytes)
+  static constexpr bool kOutF32 = kOutF32_;
+  static constexpr int kBM = 128, kBK = 128, kUmmaK = 32;
+  static constexpr int kThreads = 320;
+  static constexpr int kEpiWarps = 8;
+  static constexpr int kColsPerThread = kBN / 2;  // each epilogue thread: one row, half the tile
+  static constexpr int kChunks = kColsPerThread / 32;
+
+  static constexpr int kABytes = kBM * kBK;
+  static constexpr int kBBytes = kBN * kBK;
+  static constexpr int kSfaBytes = kMode == kModeMX ? 512 : 0;
+  static constexpr int kSfbAtoms = (kBN + 127) / 128;
+  static constexpr int kSfbBytes = kMode == kModeMX ? 512 * kSfbAtoms : 0;
+  static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
+  static constexpr int kStages = (kBN == 256) ? 4 : 6;
+
+  // TMEM: accumulator (or per-K-block partial) buffers, then the MX scales
+  static constexpr int kSfCols = kMode == kModeMX ? 4 + 4 * kSfbAtoms : 0;
+  static constexpr int kAccStages = (kMode == kModeBlk) ? 2 : ((2 * kBN + kSfCols <= 512) ? 2 : 1);
+  static constexpr int kSfaCol = kAccStages * kBN;
+  static constexpr int kSfbCol = kSfaCol + 4;
+  static constexpr int kTmemCols = 512;
+
+  // shared memory carve-up (offsets from a 1024-byte aligned base)
+  static constexpr int kOffA = 0;
+  static constexpr int kOffB = kOffA + kStages * kABytes;
+  static constexpr int kOffSfa = kOffB + kStages * kBBytes;
+  static constexpr int kOffSfb = kOffSfa + kStages * kSfaBytes;
+  static constexpr int kOffSbStage = kOffSfb + kStages * kSfbBytes;  // GROUP_N=1 column scales
+  static constexpr int kSbStageBytes = kMode == kModeBlk ? kEpiWarps * kColsPerThread * 4 : 0;
+  static constexpr int kOffBar = (kOffSbStage + kSbStageBytes + 7) / 8 * 8;
+  static constexpr int kNumBars = 2 * kStages + 2 * kAccStages + 2;
+  static constexpr int kOffCtl = kOffBar + kNumBars * 8;
+  static constexpr int kSmemBytes = kOffCtl + 16 + 1024;  // + alignment slack
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+  static_assert(kBN == 128 || kBN == 256, "tile N");
+};
+
+template <class Cfg>
+__global__ void __launch_bounds__(Cfg::kThreads, 1)
+    b2g_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                    const __grid_constant__ GemmParams p) {
+  constexpr int kMode = Cfg::kMode;
+  constexpr int kBN = Cfg::kBN;
+  constexpr int ST = Cfg::kStages;
+  constexpr int AS = Cfg::kAccStages;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + ST;
+  uint64_t* acc_full = bars + 2 * ST;
+  uint64_t* acc_empty = bars + 2 * ST + AS;
+  uint64_t* fin = bars + 2 * ST + 2 * AS;      // end-of-kernel MMA drain
+  uint64_t* never = fin + 1;                    // test hook: nothing ever arrives here
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + Cfg::kOffCtl);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kOffCtl + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (kMode == kModeMX) {  // scale atoms never fetched (tile edge) must hold a finite scale
+    for (int i = threadIdx.x; i < ST * (Cfg::kSfaBytes + Cfg::kSfbBytes) / 4; i += Cfg::kThreads)
+      reinterpret_cast<uint32_t*>(smem + Cfg::kOffSfa)[i] = 0x7F7F7F7Fu;
+    fence_proxy_async_smem();
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ST; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int s = 0; s < AS; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], Cfg::kEpiWarps); }
+    mbar_init(fin, 1);
+    mbar_init(never, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc<Cfg::kTmemCols>(tmem_holder);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const uint64_t tmo = p.timeout_ns;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_a);
+      tma_prefetch_desc(&tm_b);
+      int s = 0;
+      uint32_t ph = 0;
+      uint32_t issued_mask = 0, issued_phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < p.num_units && ok; u += gridDim.x) {
+        const Unit w = decode_unit(u, p);
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, kDevTimeoutProducer, tmo)) { ok = false; break; }
+          uint32_t tx = Cfg::kABytes + Cfg::kBBytes;
+          int nsfb = 0;
+          if (kMode == kModeMX) {
+            nsfb = p.sfb_blocks - w.nt * Cfg::kSfbAtoms;
+            nsfb = nsfb < Cfg::kSfbAtoms ? nsfb : Cfg::kSfbAtoms;
+            tx += 512u * (1 + nsfb);
+          }
+          mbar_arrive_expect_tx(&full[s], tx);
+          tma_load_3d(smem + Cfg::kOffA + s * Cfg::kABytes, &tm_a, &full[s], kb * 128, w.mt * 128, w.b);
+          if (Cfg::kBPre)
+            tma_load_5d(smem + Cfg::kOffB + s * Cfg::kBBytes, &tm_b, &full[s], 0, 0, w.nt * (kBN / 16), kb * 8, w.b);
+          else
+            tma_load_3d(smem + Cfg::kOffB + s * Cfg::kBBytes, &tm_b, &full[s], kb * 128, w.nt * kBN, w.b);
+          if (kMode == kModeMX) {
+            bulk_load(smem + Cfg::kOffSfa + s * Cfg::kSfaBytes,
+                      p.sfa + w.b * p.sfa_bstride + w.mt * p.sfa_rb + kb * 512, 512, &full[s]);
+            for (int j = 0; j < nsfb; ++j)
+              bulk_load(smem + Cfg::kOffSfb + s * Cfg::kSfbBytes + j * 512,
+                        p.sfb + w.b * p.sfb_bstride + (w.nt * Cfg::kSfbAtoms + j) * p.sfb_rb + kb * 512, 512,
+                        &full[s]);
+          }
+          issued_mask |= 1u << s;
+          issued_phase = (issued_phase & ~(1u << s)) | (ph << s);
+          if (++s == ST) { s = 0; ph ^= 1; }
+        }
+      }
+      if (*abort_flag) {  // let copies already in flight land before the CTA retires
+        for (int i = 0; i < ST; ++i)
+          if (issued_mask & (1u << i)) {
+            volatile int no_abort = 0;
+            mbar_wait(&full[i], (issued_phase >> i) & 1u, &no_abort, p.status, kDevTimeoutDrain, 100000000ull);
+          }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int s = 0, as = 0;
+      uint32_t ph = 0, aph = 0;
+      bool ok = true;
+      if (p.debug_stall) ok = mbar_wait(never, 0, abort_flag, p.status, kDevTimeoutMma, tmo);
+      for (int u = blockIdx.x; u < p.num_units && ok; u += gridDim.x) {
+        const Unit w = decode_unit(u, p);
+        if (kMode != kModeBlk) {
+          if (!mbar_wait(&acc_empty[as], aph ^ 1, abort_flag, p.status, kDevTimeoutMma, tmo)) { ok = false; break; }
+          tc_fence_after();
+        }
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
+          if (!mbar_wait(&full[s], ph, abort_flag, p.status, kDevTimeoutMma, tmo)) { ok = false; break; }
+          if (kMode == kModeBlk) {
+            if (!mbar_wait(&acc_empty[as], aph ^ 1, abort_flag, p.status, kDevTimeoutMma, tmo)) { ok = false; break; }
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smem + Cfg::kOffA + s * Cfg::kABytes);
+          const uint32_t b_base = smem_u32(smem + Cfg::kOffB + s * Cfg::kBBytes);
+          const uint32_t d_tmem = tmem_base + as * kBN;
+          if (kMode == kModeMX) {
+            tc_cp_32x128b_warpx4(tmem_base + Cfg::kSfaCol, desc_sf_atom(smem_u32(smem + Cfg::kOffSfa + s * Cfg::kSfaBytes)));
+#pragma unroll
+            for (int j = 0; j < Cfg::kSfbAtoms; ++j)
+              tc_cp_32x128b_warpx4(tmem_base + Cfg::kSfbCol + 4 * j,
+                                   desc_sf_atom(smem_u32(smem + Cfg::kOffSfb + s * Cfg::kSfbBytes + j * 512)));
+          }
+#pragma unroll
+          for (int kk = 0; kk < Cfg::kBK / Cfg::kUmmaK; ++kk) {
+            const uint64_t adesc = desc_kmajor_sw128(a_base + kk * 32);
+            const uint64_t bdesc = Cfg::kBPre ? desc_kmajor_interleave(b_base + kk * 2 * (kBN * 16), kBN * 16)
+                                              : desc_kmajor_sw128(b_base + kk * 32);
+            const uint32_t acc = (kMode == kModeBlk) ? (kk > 0) : (kb > w.kb0 || kk > 0);
+            if (kMode == kModeMX)
+              mma_mxf8f6f4(d_tmem, adesc, bdesc, idesc_mxf8f6f4(128, kBN, kk, kk), tmem_base + Cfg::kSfaCol,
+                           tmem_base + Cfg::kSfbCol, acc);
+            else
+              mma_f8f6f4(d_tmem, adesc, bdesc, idesc_f8f6f4(128, kBN), acc);
+          }
+          tc_commit(&empty[s]);  // smem stage free once these MMAs have read it
+          if (++s == ST) { s = 0; ph ^= 1; }
+          if (kMode == kModeBlk) {
+            tc_commit(&acc_full[as]);
+            if (++as == AS) { as = 0; aph ^= 1; }
+          }
+        }
+        if (!ok) break;
+        if (kMode != kModeBlk) {
+          tc_commit(&acc_full[as]);
+          if (++as == AS) { as = 0; aph ^= 1; }
+        }
+      }
+      // all MMAs retired before TMEM is released
+      tc_commit(fin);
+      volatile int no_abort = 0;
+      mbar_wait(fin, 0, &no_abort, p.status, kDevTimeoutDrain, 1000000000ull);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp - 2;
+    const int quad = warp & 3;                 // TMEM lane group this warp may access
+    const int half = ew >> 2;                  // which half of the tile's columns
+    const int row_in_tile = quad * 32 + lane;
+    const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
+    constexpr int NC = Cfg::kColsPerThread;
+    int as = 0;
+    uint32_t aph = 0;
+    float* sb_stage = reinterpret_cast<float*>(smem + Cfg::kOffSbStage) + ew * NC;
+
+    for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
+      const Unit w = decode_unit(u, p);
+      const int m = w.mt * 128 + row_in_tile;
+      const int col0 = w.nt * kBN + half * NC;
+      float acc[NC];
+      bool ok = true;
+
+      if (kMode != kModeBlk) {
+        if (!mbar_wait(&acc_full[as], aph, abort_flag, p.status, kDevTimeoutEpilogue, tmo)) break;
+        tc_fence_after();
+        uint32_t v[Cfg::kChunks][32];
+#pragma unroll
+        for (int c = 0; c < Cfg::kChunks; ++c)
+          tmem_ld_32x32b_x32(tmem_base + lane_addr + as * kBN + half * NC + c * 32, v[c]);
+        tc_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[as]);
+        if (++as == AS) { as = 0; aph ^= 1; }
+        const float alpha = p.alpha;
+#pragma unroll
+        for (int c = 0; c < Cfg::kChunks; ++c)
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[c * 32 + j] = __uint_as_float(v[c][j]) * alpha;
+      } else {
+        // fp32 block-scale promotion, one 128-K block at a time
+#pragma unroll
+        for (int j = 0; j < NC; ++j) acc[j] = 0.f;
+        const bool row_ok = m < p.M;
+        const float* sa_ptr = p.bsa + w.b * p.bsa_bstride + m;
+        const bool gn1 = p.group_n == 1;
+        const int nblk = col0 / 128;
+        const float* sb_ptr = gn1 ? (p.bsb + w.b * p.bsb_bstride + col0 + 4 * lane)
+                                  : (p.bsb + w.b * p.bsb_bstride + nblk * p.stride_sfb);
+        const bool sb_lane_ok = gn1 ? (4 * lane < NC && col0 + 4 * lane < p.N) : (col0 < p.N);
+        auto load_sa = [&](int kb) -> float { return (row_ok && kb < w.kb1) ? __ldg(sa_ptr + kb * p.stride_sfa) : 0.f; };
+        auto load_sb = [&](int kb) -> float4 {
+          float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (kb < w.kb1 && sb_lane_ok) {
+            if (gn1) r = __ldg(reinterpret_cast<const float4*>(sb_ptr + kb * p.stride_sfb));
+            else r.x = __ldg(sb_ptr + kb);
+          }
+          return r;
+        };
+        float sa0 = load_sa(w.kb0), sa1 = load_sa(w.kb0 + 1);
+        float4 sb0 = load_sb(w.kb0), sb1 = load_sb(w.kb0 + 1);
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
+          const float sa = sa0;
+          const float4 sb = sb0;
+          sa0 = sa1; sb0 = sb1;
+          sa1 = load_sa(kb + 2); sb1 = load_sb(kb + 2);
+          if (gn1) {
+            if (4 * lane < NC) *reinterpret_cast<float4*>(sb_stage + 4 * lane) = sb;
+            __syncwarp();
+          }
+          if (!mbar_wait(&acc_full[as], aph, abort_flag, p.status, kDevTimeoutEpilogue, tmo)) { ok = false; break; }
+          tc_fence_after();
+          const float s_const = sa * __shfl_sync(0xffffffffu, sb.x, 0);
+#pragma unroll
+          for (int c = 0; c < NC / 16; ++c) {  // 16-column loads keep the register budget (168) spill-free
+            uint32_t v[16];
+            tmem_ld_32x32b_x16(tmem_base + lane_addr + as * kBN + half * NC + c * 16, v);
+            tc_wait_ld();
+            if (gn1) {
+#pragma unroll
+              for (int j = 0; j < 16; j += 4) {
+                const float4 b4 = *reinterpret_cast<const float4*>(sb_stage + c * 16 + j);
+                acc[c * 16 + j + 0] = fmaf(__uint_as_float(v[j + 0]) * b4.x, sa, acc[c * 16 + j + 0]);
+                acc[c * 16 + j + 1] = fmaf(__uint_as_float(v[j + 1]) * b4.y, sa, acc[c * 16 + j + 1]);
+                acc[c * 16 + j + 2] = fmaf(__uint_as_float(v[j + 2]) * b4.z, sa, acc[c * 16 + j + 2]);
+                acc[c * 16 + j + 3] = fmaf(__uint_as_float(v[j + 3]) * b4.w, sa, acc[c * 16 + j + 3]);
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) acc[c * 16 + j] = fmaf(__uint_as_float(v[j]), s_const, acc[c * 16 + j]);
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[as]);
+          if (++as == AS) { as = 0; aph ^= 1; }
+        }
+        if (!ok) break;
+      }
+
+      // ---- write the row segment [col0, col0 + NC) of row m
+      if (m < p.M) {
+        if (p.out_mode == kOutWorkspace) {
+          float* dst = p.ws + ((static_cast<long long>(w.ks) * p.batch + w.b) * p.M + m) * static_cast<long long>(p.N);
+#pragma unroll
+          for (int j = 0; j < NC; j += 4)
+            if (col0 + j < p.N)
+              st_global_v4(dst + col0 + j, __float_as_uint(acc[j]), __float_as_uint(acc[j + 1]),
+                           __float_as_uint(acc[j + 2]), __float_as_uint(acc[j + 3]));
+        } else if (Cfg::kOutF32) {
+          float* dst = reinterpret_cast<float*>(p.c) + w.b * p.c_bstride + m * p.ldc;
+          if (p.out_mode == kOutAtomic) {
+#pragma unroll
+            for (int j = 0; j < NC; j += 4)
+              if (col0 + j < p.N) red_add_v4_f32(dst + col0 + j, acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < NC; j += 4)
+              if (col0 + j < p.N)
+                st_global_v4(dst + col0 + j, __float_as_uint(acc[j]), __float_as_uint(acc[j + 1]),
+                             __float_as_uint(acc[j + 2]), __float_as_uint(acc[j + 3]));
+          }
+        } else {
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.c) + w.b * p.c_bstride + m * p.ldc;
+#pragma unroll
+          for (int j = 0; j < NC; j += 8)
+            if (col0 + j < p.N)
+              st_global_v4(dst + col0 + j, pack_bf16x2(acc[j], acc[j + 1]), pack_bf16x2(acc[j + 2], acc[j + 3]),
+                           pack_bf16x2(acc[j + 4], acc[j + 5]), pack_bf16x2(acc[j + 6], acc[j + 7]));
+        }
+      }
+    }
+  }
+
+  // ------------------------------------------------------------ teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc<Cfg::kTmemCols>(tmem_base);
+  }
+}
+
+}  // namespace b2g

@@ -1,0 +1,176 @@
+"""torch-tensor front end over the C ABI.
+
+PyTorch supplies device memory and streams here; every computation runs in
+``libb2g.so``.  Tensors holding E4M3 / UE8M0 bytes are ``torch.uint8`` so that
+no torch fp8 semantics are involved.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import capi
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(stream) -> C.c_void_p:
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return C.c_void_p(stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream))
+
+
+def _out_code(dtype: torch.dtype) -> int:
+    if dtype == torch.bfloat16:
+        return capi.OUT_BF16
+    if dtype == torch.float32:
+        return capi.OUT_F32
+    raise ValueError(f"unsupported output dtype {dtype}")
+
+
+def sf_tc_bytes(rows: int, k: int) -> int:
+    return int(capi.lib().b2g_sf_tc_bytes(rows, k))
+
+
+def quant_mxfp8(x: torch.Tensor, sf_layout: str = "tc", stream=None):
+    """fp32 [rows, K] -> (q uint8 [rows, K], scales uint8) with scales in the
+    tensor-core atom layout ("tc", flat) or row-major [rows, K/32] ("rowmajor")."""
+    assert x.dtype == torch.float32 and x.is_cuda and x.dim() == 2
+    rows, k = x.shape
+    q = torch.empty((rows, k), dtype=torch.uint8, device=x.device)
+    sf_tc = torch.empty(sf_tc_bytes(rows, k), dtype=torch.uint8, device=x.device) if sf_layout == "tc" else None
+    sf_rm = torch.empty((rows, k // 32), dtype=torch.uint8, device=x.device) if sf_layout == "rowmajor" else None
+    capi.check(capi.lib().b2g_quant_mxfp8(x.data_ptr(), rows, k, x.stride(0), q.data_ptr(), q.stride(0),
+                                          _ptr(sf_tc), _ptr(sf_rm), _stream(stream)), "b2g_quant_mxfp8")
+    return q, (sf_tc if sf_layout == "tc" else sf_rm)
+
+
+def quant_1x128(x: torch.Tensor, stream=None):
+    rows, k = x.shape
+    q = torch.empty((rows, k), dtype=torch.uint8, device=x.device)
+    sf = torch.empty((k // 128, rows), dtype=torch.float32, device=x.device)
+    capi.check(capi.lib().b2g_quant_1x128(x.data_ptr(), rows, k, q.data_ptr(), sf.data_ptr(), _stream(stream)),
+               "b2g_quant_1x128")
+    return q, sf
+
+
+def quant_128x128(x: torch.Tensor, stream=None):
+    n, k = x.shape
+    q = torch.empty((n, k), dtype=torch.uint8, device=x.device)
+    sf = torch.empty((n // 128, k // 128), dtype=torch.float32, device=x.device)
+    capi.check(capi.lib().b2g_quant_128x128(x.data_ptr(), n, k, q.data_ptr(), sf.data_ptr(), _stream(stream)),
+               "b2g_quant_128x128")
+    return q, sf
+
+
+def sf_rowmajor_to_tc(sf: torch.Tensor, k: int, stream=None) -> torch.Tensor:
+    rows, cols = sf.shape
+    out = torch.empty(sf_tc_bytes(rows, k), dtype=torch.uint8, device=sf.device)
+    capi.check(capi.lib().b2g_sf_rowmajor_to_tc(sf.data_ptr(), rows, cols, sf.stride(0), out.data_ptr(),
+                                                _stream(stream)), "b2g_sf_rowmajor_to_tc")
+    return out
+
+
+def sf_f4gemm_to_tc(sf_shuffled: torch.Tensor, rows: int, k: int, sn: int, stream=None) -> torch.Tensor:
+    out = torch.empty(sf_tc_bytes(rows, k), dtype=torch.uint8, device=sf_shuffled.device)
+    capi.check(capi.lib().b2g_sf_f4gemm_to_tc(sf_shuffled.data_ptr(), rows, k // 32, sn, out.data_ptr(),
+                                              _stream(stream)), "b2g_sf_f4gemm_to_tc")
+    return out
+
+
+def shuffle_scale(sf: torch.Tensor, sm: int, sn: int, stream=None) -> torch.Tensor:
+    rows, cols = sf.shape
+    out = torch.empty(sm * sn, dtype=torch.uint8, device=sf.device)
+    capi.check(capi.lib().b2g_shuffle_scale(sf.data_ptr(), rows, cols, sm, sn, out.data_ptr(), _stream(stream)),
+               "b2g_shuffle_scale")
+    return out
+
+
+def shuffle_weight_16x16(w: torch.Tensor, stream=None) -> torch.Tensor:
+    n, kp = w.shape
+    out = torch.empty_like(w)
+    capi.check(capi.lib().b2g_shuffle_weight_16x16(w.data_ptr(), out.data_ptr(), n, kp, _stream(stream)),
+               "b2g_shuffle_weight_16x16")
+    return out
+
+
+def unshuffle_weight_16x16(w: torch.Tensor, stream=None) -> torch.Tensor:
+    n, kp = w.shape
+    out = torch.empty_like(w)
+    capi.check(capi.lib().b2g_unshuffle_weight_16x16(w.data_ptr(), out.data_ptr(), n, kp, _stream(stream)),
+               "b2g_unshuffle_weight_16x16")
+    return out
+
+
+def mxfp8_gemm(a: torch.Tensor, b: torch.Tensor, sfa_tc: torch.Tensor, sfb_tc: torch.Tensor,
+               out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16, alpha: float = 1.0,
+               b_preshuffled: bool = False, log2_k_split: int = 0, stream=None) -> torch.Tensor:
+    """D[M, N] = alpha * A[M, K] . B[N, K]^T, MXFP8 operands with tensor-core-layout scales."""
+    m, k = a.shape
+    n = b.shape[0]
+    if out is None:
+        out = torch.empty((m, n), dtype=out_dtype, device=a.device)
+    args = capi.Mxfp8Args(a.data_ptr(), b.data_ptr(), sfa_tc.data_ptr(), sfb_tc.data_ptr(), out.data_ptr(),
+                          m, n, k, a.stride(0), k if b_preshuffled else b.stride(0), out.stride(0), alpha,
+                          int(b_preshuffled), _out_code(out.dtype), log2_k_split)
+    capi.check(capi.lib().b2g_gemm_mxfp8(C.byref(args), _stream(stream)), "b2g_gemm_mxfp8")
+    return out
+
+
+def opus_kargs(a, b, c, sfa=None, sfb=None, stride_sfa=0, stride_sfb=0, batch=1,
+               stride_sfa_batch=0, stride_sfb_batch=0) -> capi.OpusGemmKargs:
+    """Fill opus_gemm_kargs the way the reference hosts do
+    (opus_gemm/block_scale_gemm/gemm_a8w8_blockscale_host.cc:228-247)."""
+    k = capi.OpusGemmKargs()
+    m, kk = a.shape[-2], a.shape[-1]
+    n = b.shape[-2]
+    k.ptr_a, k.ptr_b, k.ptr_c = a.data_ptr(), b.data_ptr(), c.data_ptr()
+    k.m, k.n, k.k, k.batch = m, n, kk, batch
+    k.stride_a, k.stride_b, k.stride_c = a.stride(-2), b.stride(-2), c.stride(-2)
+    k.stride_a_batch = a.stride(0) if a.dim() == 3 else m * kk
+    k.stride_b_batch = b.stride(0) if b.dim() == 3 else n * kk
+    k.stride_c_batch = c.stride(0) if c.dim() == 3 else m * n
+    k.ptr_sfa = _ptr(sfa) or 0
+    k.ptr_sfb = _ptr(sfb) or 0
+    k.stride_sfa, k.stride_sfb = stride_sfa, stride_sfb
+    k.stride_sfa_batch, k.stride_sfb_batch = stride_sfa_batch, stride_sfb_batch
+    return k
+
+
+def gemm_a8w8_blockscale(a, b, sfa, sfb, group_n: int = 128, out_dtype=torch.float32, log2_k_split: int = 0,
+                         out=None, stream=None) -> torch.Tensor:
+    """opus block_scale_gemm (group_n=128: SFB [N/128, K/128]) or
+    block_scale_1x128x1_gemm (group_n=1: SFB [K/128, N]); SFA [K/128, M]."""
+    m, kk = a.shape
+    n = b.shape[0]
+    if out is None:
+        out = torch.empty((m, n), dtype=out_dtype, device=a.device)
+    stride_sfb = (kk // 128) if group_n == 128 else sfb.stride(0)
+    ka = opus_kargs(a, b, out, sfa, sfb, stride_sfa=sfa.stride(0), stride_sfb=stride_sfb)
+    capi.check(capi.lib().b2g_gemm_a8w8_blockscale(C.byref(ka), group_n, _out_code(out.dtype), log2_k_split,
+                                                   _stream(stream)), "b2g_gemm_a8w8_blockscale")
+    return out
+
+
+def gemm_a8w8(a, b, alpha: float = 1.0, out_dtype=torch.float32, log2_k_split: int = 0, b_preshuffled=False,
+              out=None, stream=None) -> torch.Tensor:
+    m, kk = a.shape[-2], a.shape[-1]
+    n = b.shape[-2] if not b_preshuffled else b.numel() // kk
+    batch = a.shape[0] if a.dim() == 3 else 1
+    if out is None:
+        out = torch.empty((batch, m, n) if a.dim() == 3 else (m, n), dtype=out_dtype, device=a.device)
+    full = opus_kargs(a, b if not b_preshuffled else b.view(-1, n, kk), out, batch=batch)
+    ka = capi.OpusGemmKargsA8W8()
+    C.memmove(C.byref(ka), C.byref(full), C.sizeof(ka))
+    fn = capi.lib().b2g_gemm_a8w8_preshuffled if b_preshuffled else capi.lib().b2g_gemm_a8w8
+    capi.check(fn(C.byref(ka), alpha, _out_code(out.dtype), log2_k_split, _stream(stream)), "b2g_gemm_a8w8")
+    return out
+
+
+def device_status(clear: bool = True) -> int:
+    st = C.c_int(0)
+    capi.lib().b2g_device_status(C.byref(st), int(clear))
+    return st.value

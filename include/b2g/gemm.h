@@ -1,0 +1,235 @@
+/*
+ * b2g/gemm.h -- C ABI of the B200 (sm_100a) block-scaled FP8 GEMM library.
+ *
+ * Drop-in boundary for the reference's opus_gemm FP8 family and its f4gemm MX
+ * launch conventions (Fyzyukk/gcnasm).  Plain pointers, sizes and an opaque
+ * stream handle (a cudaStream_t passed as void*, NULL = legacy default stream);
+ * no torch or CUDA types in the signatures.  Every call is stream-ordered and
+ * returns a status code; the library never exits the process.
+ *
+ * Element types: A/B are OCP E4M3 bytes; MX scales are UE8M0 bytes (value
+ * 2^(e-127)); blockwise scales are fp32; C/D is bf16 (B2G_OUT_BF16) or fp32.
+ */
+#ifndef B2G_GEMM_H
+#define B2G_GEMM_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define B2G_API __attribute__((visibility("default")))
+#else
+#define B2G_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status */
+enum {
+    B2G_OK = 0,
+    B2G_ERR_INVALID_ARG = 1,    /* null pointer, non-positive size, bad enum   */
+    B2G_ERR_UNSUPPORTED = 2,    /* shape/stride outside the kernels' contract   */
+    B2G_ERR_ALIGNMENT = 3,      /* pointer or stride not 16-byte aligned        */
+    B2G_ERR_CUDA = 4,           /* a CUDA runtime/driver call failed            */
+    B2G_ERR_DEVICE_TIMEOUT = 5, /* a kernel gave up waiting (see b2g_device_status) */
+    B2G_ERR_NO_DEVICE = 6,      /* no sm_100 device current                      */
+    B2G_ERR_WORKSPACE = 7       /* split-K / layout scratch could not be obtained */
+};
+
+enum { B2G_OUT_BF16 = 0, B2G_OUT_F32 = 1 };
+
+/* --------------------------------------------------------- opus_gemm ABI */
+/* Byte-for-byte the reference's kernel argument block
+ * (opus_gemm/block_scale_gemm/gemm_a8w8_blockscale_common.h:4-25, identical in
+ * opus_gemm/block_scale_1x128x1_gemm/gemm_a8w8_1x128x1_blockscale_common.h:4-25).
+ * Strides are in elements.  SFA is fp32 [K/128, M] (stride_sfa between K groups);
+ * SFB is fp32 [N/128, K/128] for group_n = 128 (stride_sfb between N groups) or
+ * [K/128, N] for group_n = 1 (stride_sfb between K groups). */
+typedef struct opus_gemm_kargs {
+    const void* ptr_a;
+    const void* ptr_b;
+    void* ptr_c;
+    int m;
+    int n;
+    int k;
+    int batch;
+    int stride_a;
+    int stride_b;
+    int stride_c;
+    int stride_a_batch;
+    int stride_b_batch;
+    int stride_c_batch;
+    const void* ptr_sfa;
+    const void* ptr_sfb;
+    int stride_sfa;
+    int stride_sfb;
+    int stride_sfa_batch;
+    int stride_sfb_batch;
+} opus_gemm_kargs;
+
+/* The fp8_gemm kernel's argument block: the first 13 fields above
+ * (opus_gemm/fp8_gemm/gemm_a8w8_8wave.cc:99-113). */
+typedef struct opus_gemm_kargs_a8w8 {
+    const void* ptr_a;
+    const void* ptr_b;
+    void* ptr_c;
+    int m;
+    int n;
+    int k;
+    int batch;
+    int stride_a;
+    int stride_b;
+    int stride_c;
+    int stride_a_batch;
+    int stride_b_batch;
+    int stride_c_batch;
+} opus_gemm_kargs_a8w8;
+
+/* C[b] = sum_kg sfa*sfb * (A[b] . B[b]^T)_kg   with fp32 scales.
+ * Replaces the launch gemm_a8w8_blockscale_kernel<Traits><<<grid, 512>>>(kargs)
+ * (opus_gemm/block_scale_gemm/gemm_a8w8_blockscale_host.cc:257; group_n = 128)
+ * and gemm_a8w8_1x128x1_blockscale_kernel<Traits><<<...>>>(kargs)
+ * (opus_gemm/block_scale_1x128x1_gemm/gemm_a8w8_1x128x1_blockscale_host.cc:290;
+ * group_n = 1).  The reference writes fp32 C; out_dtype also allows bf16.
+ * Contract: k % 128 == 0, n % 16 == 0, stride_a/stride_b multiples of 16,
+ * 16-byte aligned A/B/C; group_n = 1 also needs stride_sfb % 4 == 0.
+ * log2_k_split: 0 = no split, > 0 = 2^L K-splits, < 0 = heuristic. */
+B2G_API int b2g_gemm_a8w8_blockscale(const opus_gemm_kargs* kargs, int group_n, int out_dtype, int log2_k_split,
+                             void* stream);
+
+/* C[b] = alpha * A[b] . B[b]^T.  Replaces gemm_a8w8_kernel<Traits><<<...>>>(kargs)
+ * (opus_gemm/fp8_gemm/gemm_a8w8_8wave.cc:780 launch, :261 kernel), which has no
+ * scale: alpha = 1.0 reproduces it.  Contract: k % 16 == 0, n % 16 == 0. */
+B2G_API int b2g_gemm_a8w8(const opus_gemm_kargs_a8w8* kargs, float alpha, int out_dtype, int log2_k_split, void* stream);
+
+/* Same with B given in the flat-mm preshuffled layout [N/16][K/16][16][16]
+ * (opus_fmm/flatmm_a8w8_gfx950.cc:638-681 shuffle_b output; kernel :244).
+ * kargs->ptr_b points at the shuffled buffer; stride_b is ignored. */
+B2G_API int b2g_gemm_a8w8_preshuffled(const opus_gemm_kargs_a8w8* kargs, float alpha, int out_dtype, int log2_k_split,
+                              void* stream);
+
+/* ------------------------------------------------------------ f4gemm ABI */
+/* The packed 0x174-byte kernel argument block of asm_f4gemm/f4gemm.hpp:64-115:
+ * every field in a 16-byte slot.  For MXFP8 one element is one byte, so the A/B
+ * strides in elements are bytes. */
+#if defined(_MSC_VER)
+#pragma pack(push, 1)
+#define B2G_PACKED
+#else
+#define B2G_PACKED __attribute__((packed))
+#endif
+typedef struct B2G_PACKED b2g_f4gemm_kargs {
+    void* ptr_D;          unsigned int _p0[2];
+    void* ptr_C;          unsigned int _p1[2];
+    void* ptr_A;          unsigned int _p2[2];
+    void* ptr_B;          unsigned int _p3[2];
+    float alpha;          unsigned int _p4[3];
+    float beta;           unsigned int _p5[3];
+    unsigned int stride_D0; unsigned int _p6[3];
+    unsigned int stride_D1; unsigned int _p7[3];
+    unsigned int stride_C0; unsigned int _p8[3];   /* used for D, as the reference kernels do */
+    unsigned int stride_C1; unsigned int _p9[3];
+    unsigned int stride_A0; unsigned int _p10[3];
+    unsigned int stride_A1; unsigned int _p11[3];
+    unsigned int stride_B0; unsigned int _p12[3];
+    unsigned int stride_B1; unsigned int _p13[3];
+    unsigned int M;       unsigned int _p14[3];
+    unsigned int N;       unsigned int _p15[3];
+    unsigned int K;       unsigned int _p16[3];
+    void* ptr_ScaleA;     unsigned int _p17[2];
+    void* ptr_ScaleB;     unsigned int _p18[2];
+    unsigned int stride_ScaleA0; unsigned int _p19[3];
+    unsigned int stride_ScaleA1; unsigned int _p20[3];
+    unsigned int stride_ScaleB0; unsigned int _p21[3];
+    unsigned int stride_ScaleB1; unsigned int _p22[3];
+    int log2_k_split;
+} b2g_f4gemm_kargs;
+#if defined(_MSC_VER)
+#pragma pack(pop)
+#endif
+
+/* D[M, N] = alpha * A[M, K] . B[N, K]^T with MXFP8 operands (E4M3, one UE8M0
+ * scale per 1x32 block of K).  Replaces Kernel::launch (asm_f4gemm/f4gemm.hpp:297-309)
+ * over the kernarg block filled by fill_args (f4gemm.hpp:355-392):
+ *   - ScaleA/ScaleB in the reference's padded + shuffled layout
+ *     (asm_f4gemm/f4gemm_ref.hpp:101-130), stride_Scale*0 = padded columns;
+ *   - bpreshuffle = 1: B in the 16x16 preshuffled layout (f4gemm_ref.hpp:78-96);
+ *   - log2_k_split > 0 splits K into 2^L parts (f4gemm.hpp:329-349); unlike the
+ *     reference's bf16 atomics the partial sums are reduced in fp32, so the
+ *     caller does NOT need to zero D first;
+ *   - beta must be 0 (ptr_C unused), the only path the reference exercises.
+ * Contract: K % 32 == 0, N % 16 == 0. */
+B2G_API int b2g_gemm_mxfp8_f4gemm(const b2g_f4gemm_kargs* args, int bpreshuffle, int out_dtype, void* stream);
+
+/* Native MXFP8 entry: scales already in the sm_100 tensor-core atom layout
+ * (b2g_sf_tc_bytes / b2g_sf_rowmajor_to_tc), so no per-call layout work.
+ * ld* in elements.  b_preshuffled: B in the 16x16 preshuffled layout. */
+typedef struct b2g_mxfp8_args {
+    const void* a;
+    const void* b;
+    const void* sfa;
+    const void* sfb;
+    void* d;
+    int m, n, k;
+    long long lda, ldb, ldd;
+    float alpha;
+    int b_preshuffled;
+    int out_dtype;
+    int log2_k_split;
+} b2g_mxfp8_args;
+
+B2G_API int b2g_gemm_mxfp8(const b2g_mxfp8_args* args, void* stream);
+
+/* ------------------------------------------------- tile selection / manifest */
+/* select_kernel (asm_f4gemm/f4gemm.hpp:210-267) over the library's own tile
+ * manifest with the reference's tie-breaks.  Writes the chosen manifest index,
+ * its tile and the log2 split; returns B2G_OK or B2G_ERR_UNSUPPORTED. */
+B2G_API int b2g_select(int m, int n, int k, int num_sm, int log2_k_split, int bpreshuffle, int* index, int* tile_m,
+               int* tile_n, int* log2_split);
+B2G_API int b2g_manifest_size(void);
+B2G_API int b2g_manifest_entry(int i, int* tile_m, int* tile_n, int* splitk, int* bpreshuffle, const char** name);
+
+/* ------------------------------------------------------ layout helpers */
+/* bytes of a UE8M0 scale buffer for `rows` rows of a K-long operand in the
+ * tensor-core atom layout (128 rows x 4 scale columns per 512-byte atom). */
+B2G_API long long b2g_sf_tc_bytes(int rows, int k);
+/* row-major [rows, cols] (leading dimension ld) -> tensor-core atom layout */
+B2G_API int b2g_sf_rowmajor_to_tc(const void* src, int rows, int cols, long long ld, void* dst, void* stream);
+/* f4gemm shuffled layout (padded columns sn) -> tensor-core atom layout */
+B2G_API int b2g_sf_f4gemm_to_tc(const void* src, int rows, int cols, int sn, void* dst, void* stream);
+/* row-major [rows, cols] -> f4gemm padded + shuffled [sm, sn] (f4gemm_ref.hpp:108-130) */
+B2G_API int b2g_shuffle_scale(const void* src, int rows, int cols, int sm, int sn, void* dst, void* stream);
+/* [N, Kp] bytes <-> 16x16 preshuffled (f4gemm_ref.hpp:81-96); N % 16 == 0, Kp % 32 == 0 */
+B2G_API int b2g_shuffle_weight_16x16(const void* src, void* dst, int n, int kp, void* stream);
+B2G_API int b2g_unshuffle_weight_16x16(const void* src, void* dst, int n, int kp, void* stream);
+
+/* ------------------------------------------------------------ quantisers */
+/* fp32 x [rows, K] (leading dim ldx) -> E4M3 q [rows, K] (leading dim ldq) and
+ * UE8M0 scales, s = 2^ceil(log2(amax/448)) per 1x32 block.  sf_tc (atom layout,
+ * b2g_sf_tc_bytes(rows, K) bytes) and/or sf_rowmajor ([rows, K/32]) may be NULL. */
+B2G_API int b2g_quant_mxfp8(const float* x, int rows, int k, long long ldx, void* q, long long ldq, void* sf_tc,
+                    void* sf_rowmajor, void* stream);
+/* 1x128 fp32 scales (amax/448), sf [K/128, rows] */
+B2G_API int b2g_quant_1x128(const float* x, int rows, int k, void* q, float* sf, void* stream);
+/* 128x128 fp32 scales, sf [N/128, K/128] */
+B2G_API int b2g_quant_128x128(const float* x, int n, int k, void* q, float* sf, void* stream);
+
+/* ------------------------------------------------------------ diagnostics */
+/* Synchronises the current device and reports (and with clear != 0 resets) the
+ * device status word the kernels write when a bounded wait gives up. */
+B2G_API int b2g_device_status(int* status, int clear);
+/* Per-wait time limit of the kernels' barrier waits, in milliseconds (default 4000). */
+B2G_API int b2g_set_wait_timeout_ms(int ms);
+/* Test hook: while on, every GEMM launch makes its MMA issuer wait on a barrier
+ * nothing arrives on, so the bounded wait runs out and the kernel reports
+ * B2G_ERR_DEVICE_TIMEOUT through b2g_device_status. */
+B2G_API int b2g_debug_force_stall(int on);
+B2G_API const char* b2g_status_string(int status);
+B2G_API const char* b2g_last_error(void);
+B2G_API int b2g_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* B2G_GEMM_H */
