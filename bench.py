@@ -1,0 +1,382 @@
+"""Benchmark: MXFP8 GEMM TFLOP/s at 8192^3 (1 GPU), M-sharded across N GPUs.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+One "step" is one MXFP8 GEMM (E4M3 A[M,K] . B[N,K]^T with one UE8M0 scale per
+1x32 K-block, fp32 accumulate, bf16 C) over inputs resident in HBM.  At N GPUs
+every rank computes an 8192-row shard of an (8192*N) x 8192 x 8192 GEMM with B
+replicated (weak scaling, no collective on the data path).  Between timed steps
+a 256 MiB buffer is written to flush L2; CUDA events bracket only the GEMM.
+
+Extra keys on the JSON line: ``roofline`` (dominant kernel, measured live),
+``cpu_baseline`` (the oracle port on the host cores, bounded sample), ``e2e``
+(through the reference-facing f4gemm C-ABI call with pinned host buffers,
+host<->device copies inside the timed region), ``decode`` (the skinny
+M=16 x N=28672 x K=4096 fp32-out split-K config as HBM GB/s), ``clocks``.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "MXFP8 GEMM TFLOP/s (% dense FP8 peak) at 8192³; HBM GB/s at M=16 decode"
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def load_traffic():
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    return json.load(open(p)) if os.path.exists(p) else {}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active," \
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown," \
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- CPU legs
+def cpu_gemm_sample(M, N, K, budget_s=12.0, seed=0):
+    """The oracle port (fp32-accumulate MX GEMM, oracle/b2g_oracle.c orc_gemm_mx, the
+    loop of asm_f4gemm/f4gemm_ref.hpp:181-222 over E4M3 x UE8M0 operands) on a
+    bounded row sample; returns (TFLOP/s, rows, cores, seconds)."""
+    import numpy as np
+
+    from oracle import oracle as O
+
+    qb, sb = O.quant_mx(O.normal_rows(5678, 0, N, K))
+    probe = 8
+    qa, sa = O.quant_mx(O.normal_rows(1234, 0, probe, K))
+    t = time.perf_counter()
+    O.gemm_mx(qa, qb, sa, sb, probe, N, K, acc_f64=False)
+    dt = time.perf_counter() - t
+    rows = int(max(probe, min(M, probe * budget_s / max(dt, 1e-6))))
+    qa, sa = O.quant_mx(O.normal_rows(1234, 0, rows, K))
+    t = time.perf_counter()
+    O.gemm_mx(qa, qb, sa, sb, rows, N, K, acc_f64=False)
+    dt = time.perf_counter() - t
+    del np
+    return 2.0 * rows * N * K / dt / 1e12, rows, O.max_threads(), dt
+
+
+# --------------------------------------------------------------------------- GPU legs
+def make_mx_operands(M, N, K, dev, seed):
+    import torch
+
+    from gcnasm_b200 import ops
+
+    g = torch.Generator(device=dev).manual_seed(seed)
+    x = torch.randn(M, K, device=dev, generator=g)
+    w = torch.randn(N, K, device=dev, generator=torch.Generator(device=dev).manual_seed(seed + 4444))
+    qa, sfa_rm = ops.quant_mxfp8(x, "rowmajor")
+    qb, sfb_rm = ops.quant_mxfp8(w, "rowmajor")
+    del x, w
+    return qa, sfa_rm, qb, sfb_rm
+
+
+def timed_steps(fn, steps, warmup, flush, stream):
+    """warmup untimed calls, then `steps` calls each bracketed by CUDA events on
+    `stream`, with an L2 flush between them (outside the events)."""
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    torch.cuda.synchronize()
+    for i in range(steps):
+        flush()
+        ev[i][0].record(stream)
+        fn()
+        ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in ev]
+
+
+def run_b200(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from gcnasm_b200 import capi, f4gemm, ops
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream()
+    peaks = load_peaks()
+    M, N, K = 8192, 8192, 8192  # this rank's shard (weak scaling: total M = 8192 * world)
+    qa, sfa_rm, qb, sfb_rm = make_mx_operands(M, N, K, dev, 1234 + rank)
+    sfa = ops.sf_rowmajor_to_tc(sfa_rm, K)
+    sfb = ops.sf_rowmajor_to_tc(sfb_rm, K)
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    flush_buf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def flush():
+        flush_buf.fill_(1)
+
+    def step():
+        ops.mxfp8_gemm(qa, qb, sfa, sfb, out=out, log2_k_split=0, stream=stream)
+
+    # correctness guard on the benchmarked data: 16 sampled rows vs the oracle
+    if rank == 0:
+        step()
+        torch.cuda.synchronize()
+        import numpy as np
+
+        from oracle import oracle as O
+
+        rows = np.arange(0, M, M // 16)
+        ref = O.gemm_mx(np.ascontiguousarray(qa.cpu().numpy()[rows]), qb.cpu().numpy(),
+                        np.ascontiguousarray(sfa_rm.cpu().numpy()[rows]), sfb_rm.cpu().numpy(), len(rows), N, K)
+        err = O.check_bf16(out[torch.from_numpy(rows).to(dev)].float().cpu().numpy(), ref)
+        if err > 1.0:
+            raise SystemExit(f"bench: GEMM output fails the bf16 tolerance (ratio {err})")
+
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    times = timed_steps(step, args.steps, args.warmup, flush, stream)
+    clk = clocks.stop()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    total_ms = sum(times)
+    t = torch.tensor([total_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+    flops_rank = 2.0 * M * N * K
+    value = flops_rank * world / (ms_per_step * 1e-3) / 1e12
+    kernel_avg_ms = statistics.mean(times)  # one GEMM kernel launch per step
+    achieved = flops_rank / (kernel_avg_ms * 1e-3) / 1e12
+    fp8_peak = 2.0 * peaks["bf16_tflops"]
+    traffic = load_traffic().get("mxfp8_8192_gemm_bytes")
+
+    result = {
+        "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "e4m3+ue8m0 (fp32 accumulate), bf16 out",
+        "data": "synthetic: torch.randn N(0,1) seeded, quantised on device with UE8M0 scales 2^ceil(log2(amax/448))",
+        "config": {"workload": "mxfp8_gemm_tn", "M": M * world, "N": N, "K": K, "M_per_gpu": M, "out": "bf16",
+                   "scales": "ue8m0 per 1x32 along K (tensor-core atom layout)", "tile": "128x256x128 persistent",
+                   "l2": "flushed between timed steps (256 MiB write, outside the events)",
+                   "parallelism": f"m-shard x{world}, B replicated, no data-path collective"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(fp8_peak, 1),
+                     "unit": "TFLOP/s", "frac": round(achieved / fp8_peak, 4),
+                     "peak_source": f"{peaks['source']} bf16 dense x2 (tcgen05 FP8 rate = 2x bf16)",
+                     "frac_of_nominal_4500": round(achieved / 4500.0, 4),
+                     "traffic": traffic, "kernel": "b2g_gemm_kernel<MX,256>"},
+        "clocks": clk,
+        "gpu_launches": args.steps,
+    }
+    if rank != 0:
+        return None
+
+    # ---------------------------------------------------------------- decode config (HBM-bound)
+    result["decode"] = bench_decode(args, dev, stream, peaks, flush)
+    # ---------------------------------------------------------------- e2e through the f4gemm C-ABI
+    result["e2e"] = bench_e2e(args, dev, stream, qa, sfa_rm, qb, sfb_rm, M, N, K)
+    del qa, qb, sfa, sfb, out
+    torch.cuda.empty_cache()
+    # ---------------------------------------------------------------- CPU baseline (oracle port)
+    tf, rows, cores, secs = cpu_gemm_sample(M, N, K, budget_s=args.cpu_budget)
+    result["cpu_baseline"] = {"value": round(tf, 5), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                              "sample": f"{rows} rows x {N} x {K} of the same GEMM ({secs:.1f} s, fp32 accumulate, "
+                                        "OpenMP over rows; extrapolates linearly in M)"}
+    del capi, f4gemm
+    return result
+
+
+def bench_decode(args, dev, stream, peaks, flush):
+    """M=16, N=28672, K=4096 MXFP8, fp32 out, split-K (C4): HBM GB/s of the GEMM."""
+    import torch
+
+    from gcnasm_b200 import ops
+
+    M, N, K = 16, 28672, 4096
+    qa, sfa_rm, qb, sfb_rm = make_mx_operands(M, N, K, dev, 77)
+    sfa, sfb = ops.sf_rowmajor_to_tc(sfa_rm, K), ops.sf_rowmajor_to_tc(sfb_rm, K)
+    out = torch.empty((M, N), dtype=torch.float32, device=dev)
+    split = args.decode_split
+
+    def step():
+        ops.mxfp8_gemm(qa, qb, sfa, sfb, out=out, log2_k_split=split, stream=stream)
+
+    times = timed_steps(step, max(args.steps, 10), args.warmup, flush, stream)
+    ms = statistics.mean(times)
+    nbytes = M * K + N * K + M * K // 32 + N * K // 32 + 4 * M * N
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    return {"M": M, "N": N, "K": K, "out": "fp32", "log2_k_split": split, "us_per_call": round(ms * 1e3, 2),
+            "hbm_gbs": round(gbs, 1), "unit": "GB/s", "peak_gbs": peaks["hbm_gbs"],
+            "frac": round(gbs / peaks["hbm_gbs"], 4), "algorithmic_bytes": nbytes,
+            "note": "includes the fp32 C zeroing memset of the split-K reduction"}
+
+
+def bench_e2e(args, dev, stream, qa, sfa_rm, qb, sfb_rm, M, N, K):
+    """The reference-facing call (b2g_gemm_mxfp8_f4gemm over the f4gemm kernarg
+    block, B 16x16-preshuffled, scales padded + shuffled) with pinned host
+    buffers: per step H2D of A, B, ScaleA, ScaleB, the call, D2H of D."""
+    import torch
+
+    from gcnasm_b200 import f4gemm, ops
+
+    sh = f4gemm.Shape(M, N, K)
+    sa_sh = ops.shuffle_scale(sfa_rm, sh.scale_a_rows(), sh.scale_cols())
+    sb_sh = ops.shuffle_scale(sfb_rm, sh.scale_b_rows(), sh.scale_cols())
+    b_sh = ops.shuffle_weight_16x16(qb)
+    h = {n: t.cpu().pin_memory() for n, t in (("A", qa), ("B", b_sh), ("SA", sa_sh), ("SB", sb_sh))}
+    d = {n: torch.empty_like(t, device=dev) for n, t in h.items()}
+    dD = torch.empty((sh.d_rows_pad(), N), dtype=torch.bfloat16, device=dev)
+    hD = torch.empty((sh.d_rows_pad(), N), dtype=torch.bfloat16).pin_memory()
+    kargs = f4gemm.fill_args(dD.data_ptr(), None, d["A"].data_ptr(), d["B"].data_ptr(), d["SA"].data_ptr(),
+                             d["SB"].data_ptr(), M, N, K, N, sh.scale_cols(), sh.scale_cols(), 1.0, 0.0, 0)
+    h2d = sum(t.numel() * t.element_size() for t in h.values())
+    d2h = hD.numel() * hD.element_size()
+
+    def step():
+        for n in h:
+            d[n].copy_(h[n], non_blocking=True)
+        f4gemm.launch(kargs, 1, stream=stream.cuda_stream)
+        hD.copy_(dD, non_blocking=True)
+
+    times = timed_steps(step, args.steps, args.warmup, lambda: None, stream)
+    ms = statistics.mean(times)
+    return {"value": round(2.0 * M * N * K / (ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 3),
+            "path": "b2g_gemm_mxfp8_f4gemm (f4gemm kernarg ABI, bpreshuffle=1, shuffled scales)"}
+
+
+def run_reference(args, rank):
+    """The reference's CPU GEMM path (oracle port; the reference itself needs hipcc
+    and aiter, absent here) on the box's host cores, bounded sample per step."""
+    if rank != 0:
+        return None
+    M = N = K = 8192
+    vals = []
+    for _ in range(args.warmup):
+        cpu_gemm_sample(M, N, K, budget_s=2.0)
+    rows_used, cores, secs_total = 0, 1, 0.0
+    for _ in range(args.steps):
+        tf, rows, cores, secs = cpu_gemm_sample(M, N, K, budget_s=args.cpu_budget / max(1, args.steps))
+        vals.append(tf)
+        rows_used, secs_total = rows, secs_total + secs
+    v = statistics.mean(vals)
+    return {"metric": METRIC, "value": round(v, 5), "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(2.0 * M * N * K / (v * 1e12) * 1e3, 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "impl": "reference",
+            "dtype": "e4m3+ue8m0 (fp32 accumulate), bf16 out", "data": "synthetic N(0,1) seeded (oracle generator)",
+            "config": {"workload": "mxfp8_gemm_tn", "M": M, "N": N, "K": K, "out": "bf16",
+                       "parallelism": "host cores (OpenMP)"},
+            "cpu_baseline": {"value": round(v, 5), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                             "sample": f"{rows_used} rows x {N} x {K} per step ({secs_total:.1f} s total); "
+                                       "time extrapolated linearly in M"},
+            "e2e": {"value": round(v, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--decode-split", type=int, default=3)
+    ap.add_argument("--cpu-budget", type=float, default=12.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        res = run_reference(args, rank)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        res = run_b200(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+    if res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

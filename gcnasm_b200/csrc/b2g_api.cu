@@ -281,6 +281,34 @@ int maybe_sync_check() {
   return B2G_OK;
 }
 
+// Tile width, split count and K-blocks per split for a request.
+int plan_tiles(const Req& r, int sms, int* bn_out, int* S_out, int* kb_per_out) {
+  int bn = r.bn, l2 = r.log2_k_split;
+  if (r.mode == kModeBlk && bn == 256) bn = 128;
+  if (bn == 0) {
+    int idx = -1, lsel = 0;
+    select_tile(r.M, r.N, sms, r.log2_k_split, r.bpre ? 1 : 0, &idx, &lsel, r.mode == kModeBlk ? 128 : 1 << 30);
+    if (idx < 0) return fail(B2G_ERR_UNSUPPORTED, "no tile in the manifest fits");
+    bn = kManifest[idx].tile_n;
+    l2 = lsel;
+  }
+  if (l2 < 0) l2 = 0;
+  if (l2 > 8) return fail(B2G_ERR_INVALID_ARG, "log2_k_split %d too large", l2);
+  const int KB = cdiv(r.K, 128);
+  int S = std::min(1 << l2, KB);
+  const int kb_per = cdiv(KB, S);
+  S = cdiv(KB, kb_per);
+  *bn_out = bn;
+  *S_out = S;
+  *kb_per_out = kb_per;
+  return B2G_OK;
+}
+
+// Scratch bytes run_gemm will ask for beyond r.ws_offset.
+size_t split_ws_bytes(const Req& r, int S) {
+  return (S > 1 && !r.out_f32) ? static_cast<size_t>(S) * r.batch * r.M * r.N * 4 : 0;
+}
+
 int run_gemm(const Req& r) {
   int rc = B2G_OK;
   if (r.M <= 0 || r.N <= 0 || r.K <= 0 || r.batch <= 0) return fail(B2G_ERR_INVALID_ARG, "non-positive problem size");
@@ -317,21 +345,10 @@ int run_gemm(const Req& r) {
   if (rc) return rc;
 
   // ---- tile + split
-  int bn = r.bn, l2 = r.log2_k_split;
-  if (r.mode == kModeBlk && bn == 256) bn = 128;
-  if (bn == 0) {
-    int idx = -1, lsel = 0;
-    select_tile(r.M, r.N, d->sms, r.log2_k_split, r.bpre ? 1 : 0, &idx, &lsel, r.mode == kModeBlk ? 128 : 1 << 30);
-    if (idx < 0) return fail(B2G_ERR_UNSUPPORTED, "no tile in the manifest fits");
-    bn = kManifest[idx].tile_n;
-    l2 = lsel;
-  }
-  if (l2 < 0) l2 = 0;
-  if (l2 > 8) return fail(B2G_ERR_INVALID_ARG, "log2_k_split %d too large", l2);
+  int bn = 0, S = 1, kb_per = 1;
+  rc = plan_tiles(r, d->sms, &bn, &S, &kb_per);
+  if (rc) return rc;
   const int KB = cdiv(r.K, 128);
-  int S = std::min(1 << l2, KB);
-  const int kb_per = cdiv(KB, S);
-  S = cdiv(KB, kb_per);
 
   GemmParams p;
   memset(&p, 0, sizeof(p));
@@ -395,7 +412,7 @@ int run_gemm(const Req& r) {
                                  static_cast<size_t>(r.N) * 4, r.M, r.stream));
   } else if (p.out_mode == kOutWorkspace) {
     void* ws = nullptr;
-    const size_t need = r.ws_offset + static_cast<size_t>(S) * r.batch * r.M * r.N * 4;
+    const size_t need = r.ws_offset + split_ws_bytes(r, S);
     rc = workspace(d, need, &ws);
     if (rc) return rc;
     p.ws = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + r.ws_offset);
@@ -580,20 +597,6 @@ int b2g_gemm_mxfp8_f4gemm(const b2g_f4gemm_kargs* a, int bpreshuffle, int out_dt
   DevState* d = nullptr;
   int rc = device_state(&d);
   if (rc) return rc;
-  const long long tcA = b2g_sf_tc_bytes(M, K), tcB = b2g_sf_tc_bytes(N, K);
-  const size_t offB = static_cast<size_t>((tcA + 255) / 256 * 256);
-  const size_t offW = offB + static_cast<size_t>((tcB + 255) / 256 * 256);
-  void* ws = nullptr;
-  rc = workspace(d, offW, &ws);
-  if (rc) return rc;
-  uint8_t* sA = static_cast<uint8_t*>(ws);
-  uint8_t* sB = sA + offB;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  b2g_sf_f4gemm_to_tc_kernel<<<grid_for(tcA, 256, d->sms), 256, 0, st>>>(
-      static_cast<const uint8_t*>(a->ptr_ScaleA), M, cols, snA, sA);
-  b2g_sf_f4gemm_to_tc_kernel<<<grid_for(tcB, 256, d->sms), 256, 0, st>>>(
-      static_cast<const uint8_t*>(a->ptr_ScaleB), N, cols, snB, sB);
-  B2G_CUDA(cudaGetLastError());
   Req r;
   r.mode = kModeMX;
   r.bpre = bpreshuffle != 0;
@@ -603,10 +606,29 @@ int b2g_gemm_mxfp8_f4gemm(const b2g_f4gemm_kargs* a, int bpreshuffle, int out_dt
   r.b = a->ptr_B; r.ldb = r.bpre ? K : static_cast<long long>(a->stride_B0);
   r.c = a->ptr_D; r.ldc = a->stride_C0;  // the reference kernels use stride_C0 for D
   r.alpha = a->alpha;
-  r.sfa = sA; r.sfb = sB;
   r.log2_k_split = a->log2_k_split;
-  r.ws_offset = offW;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
   r.stream = st;
+  // One scratch block for the re-laid-out scales and the split-K workspace,
+  // sized before anything is written into it (growing it later would free it).
+  int bn = 0, S = 1, kb_per = 1;
+  rc = plan_tiles(r, d->sms, &bn, &S, &kb_per);
+  if (rc) return rc;
+  const long long tcA = b2g_sf_tc_bytes(M, K), tcB = b2g_sf_tc_bytes(N, K);
+  const size_t offB = static_cast<size_t>((tcA + 255) / 256 * 256);
+  const size_t offW = offB + static_cast<size_t>((tcB + 255) / 256 * 256);
+  void* ws = nullptr;
+  rc = workspace(d, offW + split_ws_bytes(r, S), &ws);
+  if (rc) return rc;
+  uint8_t* sA = static_cast<uint8_t*>(ws);
+  uint8_t* sB = sA + offB;
+  b2g_sf_f4gemm_to_tc_kernel<<<grid_for(tcA, 256, d->sms), 256, 0, st>>>(
+      static_cast<const uint8_t*>(a->ptr_ScaleA), M, cols, snA, sA);
+  b2g_sf_f4gemm_to_tc_kernel<<<grid_for(tcB, 256, d->sms), 256, 0, st>>>(
+      static_cast<const uint8_t*>(a->ptr_ScaleB), N, cols, snB, sB);
+  B2G_CUDA(cudaGetLastError());
+  r.sfa = sA; r.sfb = sB;
+  r.ws_offset = offW;
   return run_gemm(r);
 }
 

@@ -390,28 +390,26 @@ ORC_API void orc_gemm_mx(const uint8_t* a, const uint8_t* b, const uint8_t* sfa,
                          float alpha, int acc_f64, float* d, int ldd)
 {
     e4m3_table();
-#pragma omp parallel for collapse(2)
+#pragma omp parallel for collapse(2) schedule(static)
     for (int i = 0; i < m; ++i) {
         for (int j = 0; j < n; ++j) {
             const uint8_t* ar = a + (int64_t)i * lda;
             const uint8_t* br = b + (int64_t)j * ldb;
-            if (acc_f64) {
-                double acc = 0.0;
-                for (int p = 0; p < k; ++p) {
-                    float va = g_e4m3[ar[p]] * orc_e8m0_to_f32(sfa[(int64_t)i * sfa_ld + p / 32]);
-                    float vb = g_e4m3[br[p]] * orc_e8m0_to_f32(sfb[(int64_t)j * sfb_ld + p / 32]);
-                    acc += (double)va * (double)vb;
+            double acc64 = 0.0;
+            float acc32 = 0.0f;
+            for (int p0 = 0; p0 < k; p0 += 32) {
+                /* the block's two scales, decoded once (same values per element) */
+                const float s_a = orc_e8m0_to_f32(sfa[(int64_t)i * sfa_ld + p0 / 32]);
+                const float s_b = orc_e8m0_to_f32(sfb[(int64_t)j * sfb_ld + p0 / 32]);
+                const int p1 = p0 + 32 < k ? p0 + 32 : k;
+                for (int p = p0; p < p1; ++p) {
+                    const float va = g_e4m3[ar[p]] * s_a;   /* dequantised element, exact */
+                    const float vb = g_e4m3[br[p]] * s_b;
+                    if (acc_f64) acc64 += (double)va * (double)vb;
+                    else acc32 += va * vb;
                 }
-                d[(int64_t)i * ldd + j] = alpha * (float)acc;
-            } else {
-                float acc = 0.0f;
-                for (int p = 0; p < k; ++p) {
-                    float va = g_e4m3[ar[p]] * orc_e8m0_to_f32(sfa[(int64_t)i * sfa_ld + p / 32]);
-                    float vb = g_e4m3[br[p]] * orc_e8m0_to_f32(sfb[(int64_t)j * sfb_ld + p / 32]);
-                    acc += va * vb;
-                }
-                d[(int64_t)i * ldd + j] = alpha * acc;
             }
+            d[(int64_t)i * ldd + j] = acc_f64 ? alpha * (float)acc64 : alpha * acc32;
         }
     }
 }

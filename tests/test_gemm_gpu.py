@@ -1,0 +1,339 @@
+"""GPU parity: every kernel path through the C ABI against the CPU oracle on the
+same seeded inputs.
+
+Tolerances (written here as asserted):
+  * bf16 C:  max |err| <= 2^-7 * max_n |ref[m, n]|     per row   (check_bf16 <= 1)
+  * fp32 C:  |err| / max(|ref|, 2^-7 * rowmax) <= 1e-3            (check_f32 <= 1e-3)
+  * quantisers, layout shuffles: bit-exact.
+The reference for MX is the oracle's f64-accumulate GEMM over dequantised
+operands (asm_f4gemm/f4gemm_ref.hpp:181-222); for the opus paths it is the f64
+form of gemm_ref (opus_gemm/*/..._host.cc gemm_ref).
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+BF16_TOL = 1.0
+F32_TOL = 1e-3
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from gcnasm_b200 import build
+    build.build()
+    return torch.device("cuda:0")
+
+
+def T(x, dev):
+    return torch.from_numpy(np.ascontiguousarray(x)).to(dev)
+
+
+def mx_operands(oracle, M, N, K, seed_a=1234, seed_b=5678):
+    x = oracle.normal_rows(seed_a, 0, M, K)
+    w = oracle.normal_rows(seed_b, 0, N, K)
+    qa, sa = oracle.quant_mx(x)
+    qb, sb = oracle.quant_mx(w)
+    return qa, sa, qb, sb
+
+
+def check_out(out, ref, out_dtype):
+    got = out.float().cpu().numpy()
+    if out_dtype == torch.bfloat16:
+        r = check_bf16(got, ref)
+        assert r <= BF16_TOL, f"bf16 error ratio {r}"
+    else:
+        r = check_f32(got, ref)
+        assert r <= F32_TOL, f"fp32 relative error {r}"
+    return r
+
+
+def check_bf16(got, ref):
+    from oracle import oracle as O
+    return O.check_bf16(got, ref)
+
+
+def check_f32(got, ref):
+    from oracle import oracle as O
+    return O.check_f32(got, ref)
+
+
+# ------------------------------------------------------------------ quantisers / layouts (bit-exact)
+@pytest.mark.parametrize("M,K", [(300, 512), (1, 32), (129, 4096)])
+def test_quant_mx_bitexact(dev, oracle, M, K):
+    from gcnasm_b200 import ops
+    x = oracle.normal_rows(1234, 0, M, K) * 3.0
+    x[0, :32] = 0.0  # all-zero block -> scale byte 1
+    q_ref, sf_ref = oracle.quant_mx(x)
+    q, sf_tc = ops.quant_mxfp8(T(x, dev), "tc")
+    q2, sf_rm = ops.quant_mxfp8(T(x, dev), "rowmajor")
+    torch.cuda.synchronize()
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+    assert np.array_equal(q2.cpu().numpy(), q_ref)
+    assert np.array_equal(sf_rm.cpu().numpy(), sf_ref)
+    assert np.array_equal(sf_tc.cpu().numpy(), oracle.sf_to_tc_layout(sf_ref))
+
+
+def test_quant_1x128_and_128x128_bitexact(dev, oracle):
+    from gcnasm_b200 import ops
+    x = oracle.normal_rows(7, 0, 256, 512)
+    q_ref, s_ref = oracle.quant_1x128(x)
+    q, s = ops.quant_1x128(T(x, dev))
+    assert np.array_equal(q.cpu().numpy(), q_ref) and np.array_equal(s.cpu().numpy(), s_ref)
+    q_ref, s_ref = oracle.quant_128x128(x)
+    q, s = ops.quant_128x128(T(x, dev))
+    assert np.array_equal(q.cpu().numpy(), q_ref) and np.array_equal(s.cpu().numpy(), s_ref)
+
+
+def test_layout_kernels_bitexact(dev, oracle):
+    from gcnasm_b200 import ops
+    rs = np.random.RandomState(5)
+    N, Kp = 96, 512
+    w = rs.randint(0, 256, (N, Kp)).astype(np.uint8)
+    ws = ops.shuffle_weight_16x16(T(w, dev))
+    assert np.array_equal(ws.cpu().numpy().ravel(), oracle.shuffle_weight_16x16(w, N, Kp))
+    assert np.array_equal(ops.unshuffle_weight_16x16(ws).cpu().numpy(), w)
+    for rows, cols in ((300, 32), (17, 8), (256, 448)):
+        sm, sn = oracle.round_up(rows, 256), oracle.round_up(cols, 8)
+        sf = rs.randint(1, 255, (rows, cols)).astype(np.uint8)
+        sh = ops.shuffle_scale(T(sf, dev), sm, sn)
+        assert np.array_equal(sh.cpu().numpy(), oracle.shuffle_scale(sf, rows, cols, sm, sn))
+        tc = ops.sf_f4gemm_to_tc(sh, rows, cols * 32, sn)
+        assert np.array_equal(tc.cpu().numpy(), oracle.sf_to_tc_layout(sf))
+        tc2 = ops.sf_rowmajor_to_tc(T(sf, dev), cols * 32)
+        assert np.array_equal(tc2.cpu().numpy(), oracle.sf_to_tc_layout(sf))
+
+
+# ------------------------------------------------------------------ MXFP8 native entry
+MX_SHAPES = [(128, 256, 128), (512, 512, 512), (300, 512, 1024), (1, 256, 256), (17, 512, 256),
+             (100, 272, 160), (256, 1024, 2048)]
+
+
+@pytest.mark.parametrize("M,N,K", MX_SHAPES)
+@pytest.mark.parametrize("out_dtype", ["bf16", "f32"])
+def test_mxfp8_native(dev, oracle, M, N, K, out_dtype):
+    from gcnasm_b200 import ops
+    od = torch.bfloat16 if out_dtype == "bf16" else torch.float32
+    qa, sa, qb, sb = mx_operands(oracle, M, N, K)
+    ref = oracle.gemm_mx(qa, qb, sa, sb, M, N, K, acc_f64=True)
+    out = ops.mxfp8_gemm(T(qa, dev), T(qb, dev), T(oracle.sf_to_tc_layout(sa), dev),
+                         T(oracle.sf_to_tc_layout(sb), dev), out_dtype=od)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    check_out(out, ref, od)
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 512, 512), (33, 1024, 1024)])
+def test_mxfp8_native_preshuffled_b(dev, oracle, M, N, K):
+    from gcnasm_b200 import ops
+    qa, sa, qb, sb = mx_operands(oracle, M, N, K)
+    ref = oracle.gemm_mx(qa, qb, sa, sb, M, N, K, acc_f64=True)
+    b_sh = T(oracle.shuffle_weight_16x16(qb, N, K).reshape(N, K), dev)
+    for bn_pre in (True,):
+        out = ops.mxfp8_gemm(T(qa, dev), b_sh, T(oracle.sf_to_tc_layout(sa), dev),
+                             T(oracle.sf_to_tc_layout(sb), dev), out_dtype=torch.float32, b_preshuffled=bn_pre)
+        torch.cuda.synchronize()
+        check_out(out, ref, torch.float32)
+
+
+@pytest.mark.parametrize("log2", [1, 2, 3])
+@pytest.mark.parametrize("out_dtype", ["bf16", "f32"])
+def test_mxfp8_splitk(dev, oracle, log2, out_dtype):
+    from gcnasm_b200 import ops
+    od = torch.bfloat16 if out_dtype == "bf16" else torch.float32
+    M, N, K = 64, 1024, 4096
+    qa, sa, qb, sb = mx_operands(oracle, M, N, K)
+    ref = oracle.gemm_mx(qa, qb, sa, sb, M, N, K, acc_f64=True)
+    out = ops.mxfp8_gemm(T(qa, dev), T(qb, dev), T(oracle.sf_to_tc_layout(sa), dev),
+                         T(oracle.sf_to_tc_layout(sb), dev), out_dtype=od, log2_k_split=log2)
+    torch.cuda.synchronize()
+    check_out(out, ref, od)
+
+
+# ------------------------------------------------------------------ f4gemm ABI (reference-facing)
+F4_SHAPES = [(128, 1024, 1024), (300, 2048, 1024), (1, 4096, 2048), (17, 512, 256), (512, 1024, 2048)]
+
+
+@pytest.mark.parametrize("M,N,K", F4_SHAPES)
+@pytest.mark.parametrize("bpre", [1, 0])
+def test_f4gemm_abi(dev, oracle, M, N, K, bpre):
+    """asm_f4gemm/run_tests.sh heuristic shapes through the reference's kernarg block."""
+    from gcnasm_b200 import f4gemm
+    sh = f4gemm.Shape(M, N, K)
+    qa, sa, qb, sb = mx_operands(oracle, M, N, K)
+    ref = oracle.gemm_mx(qa, qb, sa, sb, M, N, K, acc_f64=True)
+    hA = np.zeros((sh.a_rows_pad(), K), np.uint8); hA[:M] = qa
+    hB = np.zeros((sh.b_rows_pad(), K), np.uint8)
+    hB[:N] = oracle.shuffle_weight_16x16(qb, N, K).reshape(N, K) if bpre else qb
+    hSA = oracle.shuffle_scale(sa, M, sh.Ks(), sh.scale_a_rows(), sh.scale_cols())
+    hSB = oracle.shuffle_scale(sb, N, sh.Ks(), sh.scale_b_rows(), sh.scale_cols())
+    dA, dB, dSA, dSB = T(hA, dev), T(hB, dev), T(hSA, dev), T(hSB, dev)
+    dD = torch.zeros((sh.d_rows_pad(), N), dtype=torch.bfloat16, device=dev)
+    args = f4gemm.fill_args(dD.data_ptr(), None, dA.data_ptr(), dB.data_ptr(), dSA.data_ptr(), dSB.data_ptr(),
+                            M, N, K, N, sh.scale_cols(), sh.scale_cols(), 1.0, 0.0, 0)
+    f4gemm.launch(args, bpre)
+    torch.cuda.synchronize()
+    check_out(dD[:M], ref, torch.bfloat16)
+
+
+@pytest.mark.parametrize("split", [1, 2, 3, 4])
+def test_f4gemm_abi_splitk(dev, oracle, split):
+    """asm_f4gemm/run_tests.sh split-K sweep shape (M=256 N=1024 K=4096), log2 split 1..4."""
+    from gcnasm_b200 import f4gemm
+    M, N, K = 256, 1024, 4096
+    sh = f4gemm.Shape(M, N, K)
+    qa, sa, qb, sb = mx_operands(oracle, M, N, K)
+    ref = oracle.gemm_mx(qa, qb, sa, sb, M, N, K, acc_f64=True)
+    dA = T(qa, dev)
+    dB = T(oracle.shuffle_weight_16x16(qb, N, K).reshape(N, K), dev)
+    dSA = T(oracle.shuffle_scale(sa, M, sh.Ks(), sh.scale_a_rows(), sh.scale_cols()), dev)
+    dSB = T(oracle.shuffle_scale(sb, N, sh.Ks(), sh.scale_b_rows(), sh.scale_cols()), dev)
+    dD = torch.full((M, N), float("nan"), dtype=torch.bfloat16, device=dev)  # no zeroing needed
+    args = f4gemm.fill_args(dD.data_ptr(), None, dA.data_ptr(), dB.data_ptr(), dSA.data_ptr(), dSB.data_ptr(),
+                            M, N, K, N, sh.scale_cols(), sh.scale_cols(), 1.0, 0.0, split)
+    f4gemm.launch(args, 1)
+    torch.cuda.synchronize()
+    check_out(dD, ref, torch.bfloat16)
+
+
+# ------------------------------------------------------------------ opus block-scale paths
+@pytest.mark.parametrize("group_n", [128, 1])
+@pytest.mark.parametrize("M,N,K", [(256, 512, 256), (300, 512, 1024), (128, 1024, 2048)])
+@pytest.mark.parametrize("out_dtype", ["f32", "bf16"])
+def test_blockscale(dev, oracle, group_n, M, N, K, out_dtype):
+    from gcnasm_b200 import ops
+    od = torch.bfloat16 if out_dtype == "bf16" else torch.float32
+    x = oracle.normal_rows(1234, 0, M, K)
+    w = oracle.normal_rows(5678, 0, N, K)
+    qa, sfa = oracle.quant_1x128(x)
+    if group_n == 128:
+        qb, sfb = oracle.quant_128x128(w)
+        ref = oracle.gemm_blockscale_f64(qa, qb, sfa, sfb, M, N, K, M, K // 128, 128, 0)
+    else:
+        qb, sfb_rows = oracle.quant_1x128(w)  # [K/128, N]
+        sfb = sfb_rows
+        ref = oracle.gemm_blockscale_f64(qa, qb, sfa, sfb, M, N, K, M, N, 1, 1)
+    out = ops.gemm_a8w8_blockscale(T(qa, dev), T(qb, dev), T(sfa, dev), T(sfb, dev), group_n=group_n, out_dtype=od)
+    torch.cuda.synchronize()
+    check_out(out, ref, od)
+
+
+def test_blockscale_reference_data_recipe(dev, oracle):
+    """The reference host's own input recipe (gemm_a8w8_blockscale_host.cc:207-210:
+    A in U[0,1), B in U[-0.5,0.5), scales in U[0.8,1.2)) with its 1e-3 absolute
+    criterion (valid_vector, :46-63) on fp32 C -- seeded here."""
+    from gcnasm_b200 import ops
+    rs = np.random.RandomState(2024)
+    M, N, K = 256, 512, 256
+    a = np.array([oracle.lib().orc_f32_to_e4m3(float(v)) for v in rs.uniform(0, 1, M * K)], np.uint8).reshape(M, K)
+    b = np.array([oracle.lib().orc_f32_to_e4m3(float(v)) for v in rs.uniform(-.5, .5, N * K)], np.uint8).reshape(N, K)
+    sfa = rs.uniform(0.8, 1.2, (K // 128, M)).astype(np.float32)
+    sfb = rs.uniform(0.8, 1.2, (N // 128, K // 128)).astype(np.float32)
+    ref = oracle.gemm_blockscale(a, b, sfa, sfb, M, N, K, M, K // 128, 128, 0)
+    out = ops.gemm_a8w8_blockscale(T(a, dev), T(b, dev), T(sfa, dev), T(sfb, dev), group_n=128,
+                                   out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert float(np.abs(out.cpu().numpy() - ref).max()) <= 1e-3 * max(1.0, float(np.abs(ref).max()) / 64)
+
+
+@pytest.mark.parametrize("log2", [1, 2])
+def test_blockscale_splitk(dev, oracle, log2):
+    from gcnasm_b200 import ops
+    M, N, K = 128, 512, 2048
+    x = oracle.normal_rows(11, 0, M, K)
+    w = oracle.normal_rows(12, 0, N, K)
+    qa, sfa = oracle.quant_1x128(x)
+    qb, sfb = oracle.quant_128x128(w)
+    ref = oracle.gemm_blockscale_f64(qa, qb, sfa, sfb, M, N, K, M, K // 128, 128, 0)
+    for od in (torch.float32, torch.bfloat16):
+        out = ops.gemm_a8w8_blockscale(T(qa, dev), T(qb, dev), T(sfa, dev), T(sfb, dev), group_n=128, out_dtype=od,
+                                       log2_k_split=log2)
+        torch.cuda.synchronize()
+        check_out(out, ref, od)
+
+
+# ------------------------------------------------------------------ plain fp8 (fp8_gemm / flatmm)
+@pytest.mark.parametrize("M,N,K", [(256, 512, 256), (100, 256, 512)])
+def test_a8w8(dev, oracle, M, N, K):
+    from gcnasm_b200 import ops
+    x = oracle.normal_rows(21, 0, M, K)
+    w = oracle.normal_rows(22, 0, N, K)
+    qa = np.array([oracle.lib().orc_f32_to_e4m3(float(v)) for v in x.ravel()], np.uint8).reshape(M, K)
+    qb = np.array([oracle.lib().orc_f32_to_e4m3(float(v)) for v in w.ravel()], np.uint8).reshape(N, K)
+    ref = oracle.gemm_a8w8(qa, qb, M, N, K).astype(np.float64) * 0.5
+    out = ops.gemm_a8w8(T(qa, dev), T(qb, dev), alpha=0.5, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    check_out(out, ref, torch.float32)
+    # flat-mm form: B given [K, N] and preshuffled by the reference's shuffle_b
+    b_kn = np.ascontiguousarray(qb.T)
+    ref_kn = oracle.gemm_a8w8_kn(qa, b_kn, M, N, K).astype(np.float64)
+    b_sh = T(oracle.flatmm_shuffle_b(b_kn, N, K).reshape(N, K), dev)
+    out = ops.gemm_a8w8(T(qa, dev), b_sh, alpha=1.0, out_dtype=torch.bfloat16, b_preshuffled=True)
+    torch.cuda.synchronize()
+    check_out(out, ref_kn, torch.bfloat16)
+
+
+def test_a8w8_batched(dev, oracle):
+    from gcnasm_b200 import ops
+    B, M, N, K = 3, 128, 256, 256
+    x = oracle.normal_rows(31, 0, B * M, K).reshape(B, M, K)
+    w = oracle.normal_rows(32, 0, B * N, K).reshape(B, N, K)
+    enc = np.vectorize(lambda v: oracle.lib().orc_f32_to_e4m3(float(v)), otypes=[np.uint8])
+    qa, qb = enc(x), enc(w)
+    out = ops.gemm_a8w8(T(qa, dev), T(qb, dev), out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    for b in range(B):
+        ref = oracle.gemm_a8w8(qa[b], qb[b], M, N, K).astype(np.float64)
+        check_out(out[b], ref, torch.float32)
+
+
+# ------------------------------------------------------------------ full-size property check
+def test_mxfp8_8192_sampled_rows(dev, oracle):
+    """The headline 8192^3 MXFP8 GEMM on the GPU; 64 sampled rows recomputed by the oracle."""
+    from gcnasm_b200 import ops
+    M = N = K = 8192
+    x = torch.randn(M, K, device=dev, generator=torch.Generator(device=dev).manual_seed(1234))
+    w = torch.randn(N, K, device=dev, generator=torch.Generator(device=dev).manual_seed(5678))
+    qa, sa = ops.quant_mxfp8(x, "rowmajor")
+    qb, sb = ops.quant_mxfp8(w, "rowmajor")
+    out = ops.mxfp8_gemm(qa, qb, ops.sf_rowmajor_to_tc(sa, K), ops.sf_rowmajor_to_tc(sb, K), out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    rows = np.random.RandomState(0).choice(M, 64, replace=False)
+    qa_h, sa_h = qa.cpu().numpy(), sa.cpu().numpy()
+    ref = oracle.gemm_mx(np.ascontiguousarray(qa_h[rows]), qb.cpu().numpy(), np.ascontiguousarray(sa_h[rows]),
+                         sb.cpu().numpy(), 64, N, K, acc_f64=True)
+    check_out(out[torch.from_numpy(rows).to(dev)], ref, torch.bfloat16)
+
+
+# ------------------------------------------------------------------ bounded waits (failure detection)
+def test_bounded_wait_reports_timeout_and_context_survives(dev, oracle):
+    """A test hook makes the MMA issuer wait on a barrier nothing arrives on; the
+    wait gives up after its limit, the kernel retires cleanly, the status word
+    says so, and the next launch on the same context is correct."""
+    from gcnasm_b200 import capi, ops
+    L = capi.lib()
+    M, N, K = 128, 256, 256
+    qa, sa, qb, sb = mx_operands(oracle, M, N, K)
+    args = (T(qa, dev), T(qb, dev), T(oracle.sf_to_tc_layout(sa), dev), T(oracle.sf_to_tc_layout(sb), dev))
+    assert ops.device_status(clear=True) == 0
+    L.b2g_set_wait_timeout_ms(200)
+    L.b2g_debug_force_stall(1)
+    try:
+        ops.mxfp8_gemm(*args, out_dtype=torch.float32)
+        st = C.c_int(0)
+        rc = L.b2g_device_status(C.byref(st), 1)
+        assert rc == capi.B2G_ERR_DEVICE_TIMEOUT and st.value == 2  # kDevTimeoutMma
+    finally:
+        L.b2g_debug_force_stall(0)
+        L.b2g_set_wait_timeout_ms(4000)
+    ref = oracle.gemm_mx(qa, qb, sa, sb, M, N, K, acc_f64=True)
+    out = ops.mxfp8_gemm(*args, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    check_out(out, ref, torch.float32)
