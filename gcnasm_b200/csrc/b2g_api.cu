@@ -69,13 +69,32 @@ EncodeTiledFn encode_fn() {
 }
 
 // ------------------------------------------------------------------ per-device state
+// Kernels whose dynamic shared-memory attribute has been raised (fixed capacity,
+// no heap growth).
+struct FnCache {
+  const void* fn[64] = {};
+  int n = 0;
+};
+
 struct DevState {
   bool init = false;
   int sms = 0;
   int* status = nullptr;  // device status word written by bounded waits
   void* ws = nullptr;     // scratch: split-K workspace and per-call scale re-layout
   size_t ws_bytes = 0;
-  std::vector<const void*> configured;  // kernels whose smem attribute is set
+  FnCache fns;
+};
+
+// Where one GEMM launch gets its SM count, status word and scratch.  The
+// allocating entry points draw scratch from DevState (grown with cudaMalloc);
+// a fixed environment hands out a caller-independent buffer of fixed size.
+struct Env {
+  DevState* dev = nullptr;  // allocating path
+  int sms = 0;
+  int* status = nullptr;
+  FnCache* fns = nullptr;
+  uint8_t* fixed_ws = nullptr;  // non-null: scratch of fixed capacity, never allocated
+  size_t fixed_ws_bytes = 0;
 };
 
 std::mutex g_mu;
@@ -120,15 +139,38 @@ int workspace(DevState* d, size_t bytes, void** out) {
   return B2G_OK;
 }
 
-int ensure_smem_attr(DevState* d, const void* fn, int bytes) {
+int ensure_smem_attr(FnCache* c, const void* fn, int bytes) {
   {
     std::lock_guard<std::mutex> lk(g_mu);
-    if (std::find(d->configured.begin(), d->configured.end(), fn) != d->configured.end()) return B2G_OK;
+    for (int i = 0; i < c->n; ++i)
+      if (c->fn[i] == fn) return B2G_OK;
   }
   B2G_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
   std::lock_guard<std::mutex> lk(g_mu);
-  d->configured.push_back(fn);
+  if (c->n < 64) c->fn[c->n++] = fn;
   return B2G_OK;
+}
+
+Env env_of(DevState* d) {
+  Env e;
+  e.dev = d;
+  e.sms = d->sms;
+  e.status = d->status;
+  e.fns = &d->fns;
+  return e;
+}
+
+// Scratch of `bytes` for one call: the fixed buffer when the environment has
+// one (too small -> B2G_ERR_WORKSPACE), else the per-device grow-only block.
+int env_workspace(const Env& e, size_t bytes, void** out) {
+  if (e.fixed_ws) {
+    if (bytes > e.fixed_ws_bytes)
+      return fail(B2G_ERR_WORKSPACE, "this call needs %zu bytes of scratch; the fixed scratch array holds %zu",
+                  bytes, e.fixed_ws_bytes);
+    *out = e.fixed_ws;
+    return B2G_OK;
+  }
+  return workspace(e.dev, bytes, out);
 }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -234,10 +276,10 @@ struct Req {
 };
 
 template <class Cfg>
-int launch_cfg(DevState* d, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid,
+int launch_cfg(const Env& d, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int grid,
                cudaStream_t st) {
   const void* fn = reinterpret_cast<const void*>(&b2g_gemm_kernel<Cfg>);
-  int rc = ensure_smem_attr(d, fn, Cfg::kSmemBytes);
+  int rc = ensure_smem_attr(d.fns, fn, Cfg::kSmemBytes);
   if (rc) return rc;
   b2g_gemm_kernel<Cfg><<<grid, Cfg::kThreads, Cfg::kSmemBytes, st>>>(ta, tb, p);
   B2G_CUDA(cudaGetLastError());
@@ -245,7 +287,7 @@ int launch_cfg(DevState* d, const CUtensorMap& ta, const CUtensorMap& tb, const 
 }
 
 template <int kMode, int kBN>
-int dispatch_pre_out(DevState* d, bool pre, bool f32, const CUtensorMap& ta, const CUtensorMap& tb,
+int dispatch_pre_out(const Env& d, bool pre, bool f32, const CUtensorMap& ta, const CUtensorMap& tb,
                      const GemmParams& p, int grid, cudaStream_t st) {
   if (kMode == kModeBlk) {  // blockwise path: row-major B only
     return f32 ? launch_cfg<GemmCfg<kMode, kBN, false, true>>(d, ta, tb, p, grid, st)
@@ -260,7 +302,7 @@ int dispatch_pre_out(DevState* d, bool pre, bool f32, const CUtensorMap& ta, con
 }
 
 template <int kMode>
-int dispatch_bn(DevState* d, int bn, bool pre, bool f32, const CUtensorMap& ta, const CUtensorMap& tb,
+int dispatch_bn(const Env& d, int bn, bool pre, bool f32, const CUtensorMap& ta, const CUtensorMap& tb,
                 const GemmParams& p, int grid, cudaStream_t st) {
   // The blockwise mode keeps 128 fp32 sums per epilogue thread at kBN = 256,
   // more than the 168-register budget of a 10-warp CTA; it runs 128-wide tiles.
@@ -309,7 +351,7 @@ size_t split_ws_bytes(const Req& r, int S) {
   return (S > 1 && !r.out_f32) ? static_cast<size_t>(S) * r.batch * r.M * r.N * 4 : 0;
 }
 
-int run_gemm(const Req& r) {
+int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
   int rc = B2G_OK;
   if (r.M <= 0 || r.N <= 0 || r.K <= 0 || r.batch <= 0) return fail(B2G_ERR_INVALID_ARG, "non-positive problem size");
   if (!r.a || !r.b || !r.c) return fail(B2G_ERR_INVALID_ARG, "null A/B/C pointer");
@@ -340,13 +382,20 @@ int run_gemm(const Req& r) {
     if (r.group_n == 128 && r.stride_sfb < r.K / 128) return fail(B2G_ERR_INVALID_ARG, "stride_sfb < K/128");
   }
 
-  DevState* d = nullptr;
-  rc = device_state(&d);
-  if (rc) return rc;
+  Env env;
+  if (fixed_env) {
+    env = *fixed_env;
+  } else {
+    DevState* dst = nullptr;
+    rc = device_state(&dst);
+    if (rc) return rc;
+    env = env_of(dst);
+  }
+  const Env& d = env;
 
   // ---- tile + split
   int bn = 0, S = 1, kb_per = 1;
-  rc = plan_tiles(r, d->sms, &bn, &S, &kb_per);
+  rc = plan_tiles(r, d.sms, &bn, &S, &kb_per);
   if (rc) return rc;
   const int KB = cdiv(r.K, 128);
 
@@ -370,7 +419,7 @@ int run_gemm(const Req& r) {
   const long long units = static_cast<long long>(r.batch) * p.MT * p.NT * S;
   if (units > 0x7fffffffLL) return fail(B2G_ERR_UNSUPPORTED, "problem too large");
   p.num_units = static_cast<int>(units);
-  p.status = d->status;
+  p.status = d.status;
   p.timeout_ns = g_timeout_ns.load();
   p.debug_stall = g_force_stall.load();
 
@@ -413,12 +462,12 @@ int run_gemm(const Req& r) {
   } else if (p.out_mode == kOutWorkspace) {
     void* ws = nullptr;
     const size_t need = r.ws_offset + split_ws_bytes(r, S);
-    rc = workspace(d, need, &ws);
+    rc = env_workspace(d, need, &ws);
     if (rc) return rc;
     p.ws = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + r.ws_offset);
   }
 
-  const int grid = static_cast<int>(std::min<long long>(units, d->sms));
+  const int grid = static_cast<int>(std::min<long long>(units, d.sms));
   switch (r.mode) {
     case kModePlain: rc = dispatch_bn<kModePlain>(d, bn, r.bpre, r.out_f32, ta, tb, p, grid, r.stream); break;
     case kModeMX: rc = dispatch_bn<kModeMX>(d, bn, r.bpre, r.out_f32, ta, tb, p, grid, r.stream); break;
@@ -428,7 +477,7 @@ int run_gemm(const Req& r) {
 
   if (p.out_mode == kOutWorkspace) {
     const long long work = static_cast<long long>(r.batch) * r.M * (r.N / 4);
-    const int g = grid_for(work, 256, d->sms);
+    const int g = grid_for(work, 256, d.sms);
     if (r.out_f32)
       b2g_splitk_reduce_kernel<true><<<g, 256, 0, r.stream>>>(p.ws, r.c, S, r.batch, r.M, r.N, r.ldc, r.c_bstride);
     else
@@ -436,6 +485,55 @@ int run_gemm(const Req& r) {
     B2G_CUDA(cudaGetLastError());
   }
   return maybe_sync_check();
+}
+
+}  // namespace
+
+// =================================================================== fixed scratch
+// Device scratch for b2g_gemm_mxfp8_noalloc: a file-scope array every GPU that
+// loads this library holds until the process exits.  Bytes [0, 256) hold the
+// kernel status word; the split-K fp32 partials follow.
+static constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;  // 16 MiB
+static constexpr size_t kNoAllocStatusBytes = 256;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+
+struct NoAllocDev {
+  bool ready = false;
+  int sms = 0;
+  uint8_t* base = nullptr;  // device address of g_noalloc_scratch on this device
+  FnCache fns;
+};
+NoAllocDev g_noalloc[64];
+
+// Once per device, with that device current: look up the array's device
+// address (host code may not use the symbol itself; it is a host-side stand-in).
+int noalloc_env(Env* e) {
+  int dev = 0;
+  B2G_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return fail(B2G_ERR_NO_DEVICE, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_mu);
+  NoAllocDev& d = g_noalloc[dev];
+  if (!d.ready) {
+    int major = 0;
+    B2G_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+    if (major != 10) return fail(B2G_ERR_NO_DEVICE, "device %d is sm_%d0; this library targets sm_100a", dev, major);
+    B2G_CUDA(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev));
+    void* ptr = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (err != cudaSuccess || !ptr)
+      return fail(B2G_ERR_CUDA, "cudaGetSymbolAddress(no-alloc scratch) failed: %s", cudaGetErrorString(err));
+    d.base = static_cast<uint8_t*>(ptr);
+    d.ready = true;
+  }
+  e->dev = nullptr;
+  e->sms = d.sms;
+  e->status = reinterpret_cast<int*>(d.base);
+  e->fns = &d.fns;
+  e->fixed_ws = d.base + kNoAllocStatusBytes;
+  e->fixed_ws_bytes = kNoAllocScratchBytes - kNoAllocStatusBytes;
+  return B2G_OK;
 }
 
 }  // namespace
@@ -630,6 +728,52 @@ int b2g_gemm_mxfp8_f4gemm(const b2g_f4gemm_kargs* a, int bpreshuffle, int out_dt
   r.sfa = sA; r.sfb = sB;
   r.ws_offset = offW;
   return run_gemm(r);
+}
+
+int b2g_gemm_mxfp8_noalloc(const b2g_mxfp8_args* g, void* stream) {
+  if (!g) return fail(B2G_ERR_INVALID_ARG, "null args");
+  if (g->out_dtype != B2G_OUT_BF16 && g->out_dtype != B2G_OUT_F32) return fail(B2G_ERR_INVALID_ARG, "bad out_dtype");
+  Req r;
+  r.mode = kModeMX;
+  r.bpre = g->b_preshuffled != 0;
+  r.out_f32 = g->out_dtype == B2G_OUT_F32;
+  r.M = g->m; r.N = g->n; r.K = g->k;
+  r.a = g->a; r.lda = g->lda;
+  r.b = g->b; r.ldb = r.bpre ? g->k : g->ldb;
+  r.c = g->d; r.ldc = g->ldd;
+  r.alpha = g->alpha;
+  r.sfa = static_cast<const uint8_t*>(g->sfa);
+  r.sfb = static_cast<const uint8_t*>(g->sfb);
+  r.log2_k_split = g->log2_k_split;
+  r.stream = static_cast<cudaStream_t>(stream);
+  if (r.M <= 0 || r.N <= 0 || r.K <= 0) return fail(B2G_ERR_INVALID_ARG, "non-positive problem size");
+  Env e;
+  int rc = noalloc_env(&e);
+  if (rc) return rc;
+  // reject up front, before any device work is queued, if the partials do not fit
+  int bn = 0, S = 1, kb_per = 1;
+  rc = plan_tiles(r, e.sms, &bn, &S, &kb_per);
+  if (rc) return rc;
+  const size_t need = split_ws_bytes(r, S);
+  if (need > e.fixed_ws_bytes)
+    return fail(B2G_ERR_WORKSPACE,
+                "b2g_gemm_mxfp8_noalloc: %d-way split-K partials need %zu bytes; its fixed scratch holds %zu "
+                "(use a smaller log2_k_split, fp32 output, or b2g_gemm_mxfp8)", S, need, e.fixed_ws_bytes);
+  // the status word must start at zero; the partials are fully overwritten
+  B2G_CUDA(cudaMemsetAsync(e.status, 0, sizeof(int), r.stream));
+  rc = run_gemm(r, &e);
+  if (rc) return rc;
+  static const bool sync_check = [] {
+    const char* v = getenv("B2G_SYNC_CHECK");
+    return v && v[0] == '1';
+  }();
+  if (sync_check) {
+    int st = 0;
+    B2G_CUDA(cudaStreamSynchronize(r.stream));
+    B2G_CUDA(cudaMemcpy(&st, e.status, sizeof(int), cudaMemcpyDeviceToHost));
+    if (st) return fail(B2G_ERR_DEVICE_TIMEOUT, "kernel reported device status %d", st);
+  }
+  return B2G_OK;
 }
 
 // ------------------------------------------------------------ layout helpers

@@ -181,6 +181,24 @@ typedef struct b2g_mxfp8_args {
 
 B2G_API int b2g_gemm_mxfp8(const b2g_mxfp8_args* args, void* stream);
 
+/* b2g_gemm_mxfp8 for callers that cannot allocate device memory.  No counterpart
+ * in the reference (its host programs own every buffer and its kernels need no
+ * scratch).  Some hosts hand all of the GPU's memory to their own pool at start-up
+ * (serving engines, frameworks with a caching allocator): a cudaMalloc made inside
+ * a library either fails for lack of free memory or hides memory the pool cannot
+ * account for or reclaim.  This entry point allocates nothing: the split-K fp32
+ * partials (bf16 output with log2_k_split > 0) live in a fixed 16 MiB array that
+ * the library declares at file scope, which every GPU that loads the library holds
+ * until the process exits.  The caller still passes A, B, the scales and D.
+ *   - The first call on a device looks up that array's device address; make that
+ *     first call before any stream capture.
+ *   - Split-K partials needing more than 16 MiB - 256 B (S * M * N * 4 bytes) are
+ *     rejected with B2G_ERR_WORKSPACE before any device work is queued.
+ *   - Every call on a device shares the one array: calls that overlap on the GPU
+ *     (concurrent streams) race on it and must be serialised by the caller.
+ * It never calls cudaMalloc, cudaFree or any allocating routine. */
+B2G_API int b2g_gemm_mxfp8_noalloc(const b2g_mxfp8_args* args, void* stream);
+
 /* ------------------------------------------------- tile selection / manifest */
 /* select_kernel (asm_f4gemm/f4gemm.hpp:210-267) over the library's own tile
  * manifest with the reference's tie-breaks.  Writes the chosen manifest index,
