@@ -443,14 +443,13 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
     rc = encode(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, r.b, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   } else {
-    // [N/16][K/16][16 rows][16 bytes] viewed as (k16, n16, n_grp, k_grp, batch) so
-    // that a box lands in smem as [k_grp][n][16 B]: the interleaved K-major
-    // operand layout of tcgen05.mma.
-    cuuint64_t dims[5] = {16, 16, (cuuint64_t)(r.N / 16), (cuuint64_t)(r.K / 16), (cuuint64_t)r.batch};
-    cuuint64_t str[4] = {16, (cuuint64_t)16 * r.K, 256,
-                         (cuuint64_t)(r.batch > 1 ? r.b_bstride : (long long)r.N * r.K)};
-    cuuint32_t box[5] = {16, 16, (cuuint32_t)(bn / 16), 8, 1};
-    rc = encode(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 5, r.b, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+    // [N/16][K/16][16 rows x 16 bytes] viewed as (256-byte tile, n_grp, k_grp, batch):
+    // a box of (256, BN/16, 8, 1) lands in smem as [k_grp][n][16 B], the interleaved
+    // K-major operand layout of tcgen05.mma, with 256 contiguous bytes per request.
+    cuuint64_t dims[4] = {256, (cuuint64_t)(r.N / 16), (cuuint64_t)(r.K / 16), (cuuint64_t)r.batch};
+    cuuint64_t str[3] = {(cuuint64_t)16 * r.K, 256, (cuuint64_t)(r.batch > 1 ? r.b_bstride : (long long)r.N * r.K)};
+    cuuint32_t box[4] = {256, (cuuint32_t)(bn / 16), 8, 1};
+    rc = encode(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, r.b, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
   }
 

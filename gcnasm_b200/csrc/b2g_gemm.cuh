@@ -200,7 +200,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
           mbar_arrive_expect_tx(&full[s], tx);
           tma_load_3d(smem + Cfg::kOffA + s * Cfg::kABytes, &tm_a, &full[s], kb * 128, w.mt * 128, w.b);
           if (Cfg::kBPre)
-            tma_load_5d(smem + Cfg::kOffB + s * Cfg::kBBytes, &tm_b, &full[s], 0, 0, w.nt * (kBN / 16), kb * 8, w.b);
+            tma_load_4d(smem + Cfg::kOffB + s * Cfg::kBBytes, &tm_b, &full[s], 0, w.nt * (kBN / 16), kb * 8, w.b);
           else
             tma_load_3d(smem + Cfg::kOffB + s * Cfg::kBBytes, &tm_b, &full[s], kb * 128, w.nt * kBN, w.b);
           if (kMode == kModeMX) {

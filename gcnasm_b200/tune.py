@@ -142,7 +142,6 @@ def main(argv=None):
     if st:
         print(f"device status {st}", file=sys.stderr)
         return 1
-    del statistics
     return 0
 
 
