@@ -21,6 +21,7 @@
 
 #include "b2g_aux.cuh"
 #include "b2g_gemm.cuh"
+#include "b2g_gemm_pair.cuh"
 
 using namespace b2g;
 
@@ -187,11 +188,14 @@ struct TileCfg {
 };
 // Same columns as the reference manifest f4gemm_bf16_per1x32Fp4.csv
 // (tile_M, tile_N, splitK, bpreshuffle, knl_name), one row per kernel variant.
+// tile_M = 256 rows are the CTA-pair kernel (two SMs per tile).
 const TileCfg kManifest[] = {
     {128, 256, 1, 0, "b2g_sm100a_fp8_128x256"},
     {128, 128, 1, 0, "b2g_sm100a_fp8_128x128"},
     {128, 256, 1, 1, "b2g_sm100a_fp8_128x256_bpreshuffle"},
     {128, 128, 1, 1, "b2g_sm100a_fp8_128x128_bpreshuffle"},
+    {256, 256, 1, 0, "b2g_sm100a_fp8_pair_256x256"},
+    {256, 256, 1, 1, "b2g_sm100a_fp8_pair_256x256_bpreshuffle"},
 };
 constexpr int kManifestN = sizeof(kManifest) / sizeof(kManifest[0]);
 
@@ -310,6 +314,43 @@ int dispatch_bn(const Env& d, int bn, bool pre, bool f32, const CUtensorMap& ta,
   return dispatch_pre_out<kMode, 128>(d, pre, f32, ta, tb, p, grid, st);
 }
 
+template <class Cfg>
+int launch_pair(const Env& d, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tsa,
+                const CUtensorMap& tsb, const PairParams& pp, cudaStream_t st) {
+  const void* fn = reinterpret_cast<const void*>(&b2g_gemm_pair_kernel<Cfg>);
+  int rc = ensure_smem_attr(d.fns, fn, Cfg::kSmemBytes);
+  if (rc) return rc;
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(2 * pp.num_pairs, 1, 1);
+  cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  B2G_CUDA(cudaLaunchKernelEx(&cfg, b2g_gemm_pair_kernel<Cfg>, ta, tb, tsa, tsb, pp));
+  return B2G_OK;
+}
+
+int dispatch_pair(const Env& d, int mode, bool pre, bool f32, const CUtensorMap& ta, const CUtensorMap& tb,
+                  const CUtensorMap& tsa, const CUtensorMap& tsb, const PairParams& pp, cudaStream_t st) {
+  if (mode == kModeMX) {
+    if (pre) return f32 ? launch_pair<PairCfg<kModeMX, true, true>>(d, ta, tb, tsa, tsb, pp, st)
+                        : launch_pair<PairCfg<kModeMX, true, false>>(d, ta, tb, tsa, tsb, pp, st);
+    return f32 ? launch_pair<PairCfg<kModeMX, false, true>>(d, ta, tb, tsa, tsb, pp, st)
+               : launch_pair<PairCfg<kModeMX, false, false>>(d, ta, tb, tsa, tsb, pp, st);
+  }
+  if (pre) return f32 ? launch_pair<PairCfg<kModePlain, true, true>>(d, ta, tb, tsa, tsb, pp, st)
+                      : launch_pair<PairCfg<kModePlain, true, false>>(d, ta, tb, tsa, tsb, pp, st);
+  return f32 ? launch_pair<PairCfg<kModePlain, false, true>>(d, ta, tb, tsa, tsb, pp, st)
+             : launch_pair<PairCfg<kModePlain, false, false>>(d, ta, tb, tsa, tsb, pp, st);
+}
+
 int maybe_sync_check() {
   static const bool on = [] {
     const char* e = getenv("B2G_SYNC_CHECK");
@@ -324,16 +365,25 @@ int maybe_sync_check() {
 }
 
 // Tile width, split count and K-blocks per split for a request.
-int plan_tiles(const Req& r, int sms, int* bn_out, int* S_out, int* kb_per_out) {
-  int bn = r.bn, l2 = r.log2_k_split;
+int plan_tiles(const Req& r, int sms, int* bn_out, int* S_out, int* kb_per_out, int* bm_out = nullptr) {
+  int bn = r.bn, l2 = r.log2_k_split, bm = 128;
   if (r.mode == kModeBlk && bn == 256) bn = 128;
   if (bn == 0) {
     int idx = -1, lsel = 0;
     select_tile(r.M, r.N, sms, r.log2_k_split, r.bpre ? 1 : 0, &idx, &lsel, r.mode == kModeBlk ? 128 : 1 << 30);
     if (idx < 0) return fail(B2G_ERR_UNSUPPORTED, "no tile in the manifest fits");
     bn = kManifest[idx].tile_n;
+    bm = kManifest[idx].tile_m;
     l2 = lsel;
   }
+  // The pair tile wastes half its rows at M <= 128 (and the blockwise mode has no
+  // pair kernel): those run the single-CTA 128 x 256 tile.
+  static const bool pair_off = [] {
+    const char* v = getenv("B2G_DISABLE_PAIR");
+    return v && v[0] == '1';
+  }();
+  if (bm == 256 && (r.M <= 128 || r.mode == kModeBlk || pair_off)) bm = 128;
+  if (bm_out) *bm_out = bm;
   if (l2 < 0) l2 = 0;
   if (l2 > 8) return fail(B2G_ERR_INVALID_ARG, "log2_k_split %d too large", l2);
   const int KB = cdiv(r.K, 128);
@@ -394,9 +444,10 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
   const Env& d = env;
 
   // ---- tile + split
-  int bn = 0, S = 1, kb_per = 1;
-  rc = plan_tiles(r, d.sms, &bn, &S, &kb_per);
+  int bn = 0, S = 1, kb_per = 1, bm = 128;
+  rc = plan_tiles(r, d.sms, &bn, &S, &kb_per, &bm);
   if (rc) return rc;
+  const bool pair = bm == 256;
   const int KB = cdiv(r.K, 128);
 
   GemmParams p;
@@ -413,7 +464,7 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
   p.stride_sfa = r.stride_sfa; p.stride_sfb = r.stride_sfb;
   p.bsa_bstride = r.bsa_bstride; p.bsb_bstride = r.bsb_bstride;
   p.group_n = r.group_n;
-  p.MT = cdiv(r.M, 128); p.NT = cdiv(r.N, bn);
+  p.MT = cdiv(r.M, bm); p.NT = cdiv(r.N, bn);
   p.S = S; p.KB = KB; p.kb_per_split = kb_per;
   p.group_m = 8;
   const long long units = static_cast<long long>(r.batch) * p.MT * p.NT * S;
@@ -439,7 +490,7 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
   if (!r.bpre) {
     cuuint64_t dims[3] = {(cuuint64_t)r.K, (cuuint64_t)r.N, (cuuint64_t)r.batch};
     cuuint64_t str[2] = {(cuuint64_t)r.ldb, (cuuint64_t)(r.batch > 1 ? r.b_bstride : r.ldb * r.N)};
-    cuuint32_t box[3] = {128, (cuuint32_t)bn, 1};
+    cuuint32_t box[3] = {128, (cuuint32_t)(pair ? 128 : bn), 1};  // a pair CTA loads 128 of the 256 B rows
     rc = encode(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, r.b, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   } else {
@@ -448,7 +499,7 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
     // K-major operand layout of tcgen05.mma, with 256 contiguous bytes per request.
     cuuint64_t dims[4] = {256, (cuuint64_t)(r.N / 16), (cuuint64_t)(r.K / 16), (cuuint64_t)r.batch};
     cuuint64_t str[3] = {(cuuint64_t)16 * r.K, 256, (cuuint64_t)(r.batch > 1 ? r.b_bstride : (long long)r.N * r.K)};
-    cuuint32_t box[4] = {256, (cuuint32_t)(bn / 16), 8, 1};
+    cuuint32_t box[4] = {256, (cuuint32_t)((pair ? 128 : bn) / 16), 8, 1};
     rc = encode(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, r.b, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
   }
@@ -466,6 +517,31 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
     p.ws = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + r.ws_offset);
   }
 
+  if (pair) {
+    // scale atoms as (128 words, k-block, row block, batch) boxes
+    CUtensorMap tsa, tsb;
+    memset(&tsa, 0, sizeof(tsa));
+    memset(&tsb, 0, sizeof(tsb));
+    if (r.mode == kModeMX) {
+      const long long kb4 = cdiv(r.K, 128);
+      for (int which = 0; which < 2; ++which) {
+        const int rows = which ? r.N : r.M;
+        const long long rb = cdiv(rows, 128);
+        const long long bstr = which ? r.sfb_bstride : r.sfa_bstride;
+        cuuint64_t dims[4] = {128, (cuuint64_t)kb4, (cuuint64_t)rb, (cuuint64_t)r.batch};
+        cuuint64_t str[3] = {512, (cuuint64_t)(kb4 * 512), (cuuint64_t)(r.batch > 1 ? bstr : rb * kb4 * 512)};
+        cuuint32_t box[4] = {128, 1, (cuuint32_t)(which ? 2 : 1), 1};
+        rc = encode(which ? &tsb : &tsa, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, which ? (const void*)r.sfb : (const void*)r.sfa,
+                    dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (rc) return rc;
+      }
+    }
+    PairParams pp;
+    pp.g = p;
+    pp.num_pairs = static_cast<int>(std::min<long long>(units, d.sms / 2));
+    rc = dispatch_pair(d, r.mode, r.bpre, r.out_f32, ta, tb, tsa, tsb, pp, r.stream);
+    if (rc) return rc;
+  } else {
   const int grid = static_cast<int>(std::min<long long>(units, d.sms));
   switch (r.mode) {
     case kModePlain: rc = dispatch_bn<kModePlain>(d, bn, r.bpre, r.out_f32, ta, tb, p, grid, r.stream); break;
@@ -473,6 +549,7 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
     default: rc = dispatch_bn<kModeBlk>(d, bn, r.bpre, r.out_f32, ta, tb, p, grid, r.stream); break;
   }
   if (rc) return rc;
+  }
 
   if (p.out_mode == kOutWorkspace) {
     const long long work = static_cast<long long>(r.batch) * r.M * (r.N / 4);

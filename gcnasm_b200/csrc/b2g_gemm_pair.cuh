@@ -1,0 +1,283 @@
+// b2g_gemm_pair.cuh -- CTA-pair (cluster of 2) variant of the persistent FP8 GEMM.
+//
+// Tile 256 x 256 x 128 per pair; tcgen05.mma.cta_group::2 with M = 256: CTA r of
+// the pair holds A rows [r*128, r*128 + 128) and B rows [r*128, r*128 + 128) of
+// the tile in its own shared memory and receives the 128 x 256 accumulator of
+// its A rows in its own TMEM.  Per SM and 128-K block that is 32 KB of operands
+// for 128 x 256 x 128 MACs, two thirds of the 48 KB the single-CTA 128 x 256
+// tile needs, which lets the ring hold 6 stages.
+//
+// Protocol (leader = cluster rank 0):
+//   * both CTAs allocate TMEM with cta_group::2 and free it after a cluster sync;
+//   * both CTAs' producers wait on their own `empty` ring and issue TMA loads
+//     into their own smem whose completion is counted on the LEADER's `full`
+//     barrier (cp.async.bulk.tensor ... .cta_group::2); the leader arms it with
+//     the bytes of both CTAs;
+//   * the leader's single MMA thread issues the MMAs (and, for MX, the
+//     tcgen05.cp of both CTAs' scale atoms) and commits with a multicast arrival
+//     on both CTAs' `empty` / `acc_full` barriers;
+//   * both CTAs' epilogues drain their own TMEM and arrive on the leader's
+//     `acc_empty` (16 arrivals: 8 warps x 2 CTAs).
+// No TMA load uses .multicast::cluster and no kernel reads another GPU's memory.
+#pragma once
+
+#include "b2g_gemm.cuh"
+
+namespace b2g {
+
+template <int kMode_, bool kBPre_, bool kOutF32_>
+struct PairCfg {
+  static constexpr int kMode = kMode_;
+  static constexpr bool kBPre = kBPre_;
+  static constexpr bool kOutF32 = kOutF32_;
+  static constexpr int kBN = 256;     // pair tile N (MMA N)
+  static constexpr int kHalf = 128;   // rows of A and of B per CTA
+  static constexpr int kThreads = 320;
+  static constexpr int kEpiWarps = 8;
+  static constexpr int kColsPerThread = kBN / 2;
+  static constexpr int kChunks = kColsPerThread / 32;
+
+  static constexpr int kABytes = kHalf * 128;
+  static constexpr int kBBytes = kHalf * 128;
+  static constexpr int kSfaBytes = kMode == kModeMX ? 512 : 0;
+  static constexpr int kSfbBytes = kMode == kModeMX ? 1024 : 0;  // both B row blocks of the pair tile
+  static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
+  static constexpr int kStages = 6;
+  static constexpr uint32_t kTxPerStage = 2u * kStageBytes;  // both CTAs complete on the leader's barrier
+
+  static constexpr int kSfCols = kMode == kModeMX ? 12 : 0;
+  static constexpr int kAccStages = (2 * kBN + kSfCols <= 512) ? 2 : 1;
+  static constexpr int kSfaCol = kAccStages * kBN;
+  static constexpr int kSfbCol = kSfaCol + 4;
+  static constexpr int kTmemCols = 512;
+
+  static constexpr int kOffA = 0;
+  static constexpr int kOffB = kOffA + kStages * kABytes;
+  static constexpr int kOffSfa = kOffB + kStages * kBBytes;
+  static constexpr int kOffSfb = kOffSfa + kStages * kSfaBytes;
+  static constexpr int kOffBar = (kOffSfb + kStages * kSfbBytes + 7) / 8 * 8;
+  static constexpr int kNumBars = 2 * kStages + 2 * kAccStages + 2;
+  static constexpr int kOffCtl = kOffBar + kNumBars * 8;
+  static constexpr int kSmemBytes = kOffCtl + 16 + 1024;
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
+
+struct PairParams {
+  GemmParams g;      // shapes, output, scales, diagnostics (MT counts 256-row pair tiles)
+  int num_pairs;     // gridDim.x / 2
+};
+
+template <class Cfg>
+__global__ void __launch_bounds__(Cfg::kThreads, 1)
+    b2g_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                         const __grid_constant__ CUtensorMap tm_sfa, const __grid_constant__ CUtensorMap tm_sfb,
+                         const __grid_constant__ PairParams pp) {
+  constexpr int kMode = Cfg::kMode;
+  constexpr int ST = Cfg::kStages;
+  constexpr int AS = Cfg::kAccStages;
+  constexpr int kBN = Cfg::kBN;
+  const GemmParams& p = pp.g;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + ST;
+  uint64_t* acc_full = bars + 2 * ST;
+  uint64_t* acc_empty = bars + 2 * ST + AS;
+  uint64_t* fin = bars + 2 * ST + 2 * AS;
+  uint64_t* never = fin + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + Cfg::kOffCtl);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kOffCtl + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ST; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int s = 0; s < AS; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], 2 * Cfg::kEpiWarps); }
+    mbar_init(fin, 1);
+    mbar_init(never, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc_pair<Cfg::kTmemCols>(tmem_holder);
+  tc_fence_before();
+  cluster_sync_all();  // barriers initialised in both CTAs before any remote access
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const uint64_t tmo = p.timeout_ns;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_a);
+      tma_prefetch_desc(&tm_b);
+      if (kMode == kModeMX) { tma_prefetch_desc(&tm_sfa); tma_prefetch_desc(&tm_sfb); }
+      int s = 0;
+      uint32_t ph = 0;
+      uint32_t issued_mask = 0, issued_phase = 0;
+      bool ok = true;
+      for (int u = pair; u < p.num_units && ok; u += pp.num_pairs) {
+        const Unit w = decode_unit(u, p);
+        const int arow = w.mt * 256 + static_cast<int>(rank) * 128;  // this CTA's A rows
+        const int brow = w.nt * kBN + static_cast<int>(rank) * 128;  // this CTA's B rows
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, kDevTimeoutProducer, tmo)) { ok = false; break; }
+          const uint32_t bar = mapa_shared(smem_u32(&full[s]), 0);
+          if (leader) mbar_arrive_expect_tx(&full[s], Cfg::kTxPerStage);
+          tma_load_3d_pair(smem + Cfg::kOffA + s * Cfg::kABytes, &tm_a, bar, kb * 128, arow, w.b);
+          if (Cfg::kBPre)
+            tma_load_4d_pair(smem + Cfg::kOffB + s * Cfg::kBBytes, &tm_b, bar, 0, brow / 16, kb * 8, w.b);
+          else
+            tma_load_3d_pair(smem + Cfg::kOffB + s * Cfg::kBBytes, &tm_b, bar, kb * 128, brow, w.b);
+          if (kMode == kModeMX) {
+            // scale atoms: (128 words, k-block, row block) boxes of the atom-layout buffers
+            tma_load_4d_pair(smem + Cfg::kOffSfa + s * Cfg::kSfaBytes, &tm_sfa, bar, 0, kb, w.mt * 2 + rank, w.b);
+            tma_load_4d_pair(smem + Cfg::kOffSfb + s * Cfg::kSfbBytes, &tm_sfb, bar, 0, kb, w.nt * 2, w.b);
+          }
+          issued_mask |= 1u << s;
+          issued_phase = (issued_phase & ~(1u << s)) | (ph << s);
+          if (++s == ST) { s = 0; ph ^= 1; }
+        }
+      }
+      if (*abort_flag) {
+        if (leader) {  // the leader's barriers count both CTAs' copies
+          for (int i = 0; i < ST; ++i)
+            if (issued_mask & (1u << i)) {
+              volatile int no_abort = 0;
+              mbar_wait(&full[i], (issued_phase >> i) & 1u, &no_abort, p.status, kDevTimeoutDrain, 100000000ull);
+            }
+        } else {  // copies signal the leader; give any in flight time to land
+          const uint64_t t0 = globaltimer_ns();
+          while (globaltimer_ns() - t0 < 2000000ull) sleep_ns(10000);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    if (leader && lane == 0) {
+      int s = 0, as = 0;
+      uint32_t ph = 0, aph = 0;
+      bool ok = true;
+      constexpr uint16_t kBoth = 0x3;
+      if (p.debug_stall) ok = mbar_wait(never, 0, abort_flag, p.status, kDevTimeoutMma, tmo);
+      for (int u = pair; u < p.num_units && ok; u += pp.num_pairs) {
+        const Unit w = decode_unit(u, p);
+        if (!mbar_wait(&acc_empty[as], aph ^ 1, abort_flag, p.status, kDevTimeoutMma, tmo)) { ok = false; break; }
+        tc_fence_after();
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
+          if (!mbar_wait(&full[s], ph, abort_flag, p.status, kDevTimeoutMma, tmo)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(smem + Cfg::kOffA + s * Cfg::kABytes);
+          const uint32_t b_base = smem_u32(smem + Cfg::kOffB + s * Cfg::kBBytes);
+          const uint32_t d_tmem = tmem_base + as * kBN;
+          if (kMode == kModeMX) {
+            tc_cp_32x128b_warpx4_pair(tmem_base + Cfg::kSfaCol,
+                                      desc_sf_atom(smem_u32(smem + Cfg::kOffSfa + s * Cfg::kSfaBytes)));
+            tc_cp_32x128b_warpx4_pair(tmem_base + Cfg::kSfbCol,
+                                      desc_sf_atom(smem_u32(smem + Cfg::kOffSfb + s * Cfg::kSfbBytes)));
+            tc_cp_32x128b_warpx4_pair(tmem_base + Cfg::kSfbCol + 4,
+                                      desc_sf_atom(smem_u32(smem + Cfg::kOffSfb + s * Cfg::kSfbBytes + 512)));
+          }
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t adesc = desc_kmajor_sw128(a_base + kk * 32);
+            const uint64_t bdesc = Cfg::kBPre ? desc_kmajor_interleave(b_base + kk * 2 * (Cfg::kHalf * 16), Cfg::kHalf * 16)
+                                              : desc_kmajor_sw128(b_base + kk * 32);
+            const uint32_t acc = (kb > w.kb0 || kk > 0);
+            if (kMode == kModeMX)
+              mma_mxf8f6f4_pair(d_tmem, adesc, bdesc, idesc_mxf8f6f4(256, kBN, kk, kk), tmem_base + Cfg::kSfaCol,
+                                tmem_base + Cfg::kSfbCol, acc);
+            else
+              mma_f8f6f4_pair(d_tmem, adesc, bdesc, idesc_f8f6f4(256, kBN), acc);
+          }
+          tc_commit_pair_mc(&empty[s], kBoth);
+          if (++s == ST) { s = 0; ph ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit_pair_mc(&acc_full[as], kBoth);
+        if (++as == AS) { as = 0; aph ^= 1; }
+      }
+      tc_commit_pair(fin);
+      volatile int no_abort = 0;
+      mbar_wait(fin, 0, &no_abort, p.status, kDevTimeoutDrain, 1000000000ull);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int ew = warp - 2;
+    const int quad = warp & 3;
+    const int half = ew >> 2;
+    const int row_in_tile = static_cast<int>(rank) * 128 + quad * 32 + lane;
+    const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
+    constexpr int NC = Cfg::kColsPerThread;
+    int as = 0;
+    uint32_t aph = 0;
+    for (int u = pair; u < p.num_units; u += pp.num_pairs) {
+      const Unit w = decode_unit(u, p);
+      const int m = w.mt * 256 + row_in_tile;
+      const int col0 = w.nt * kBN + half * NC;
+      if (!mbar_wait(&acc_full[as], aph, abort_flag, p.status, kDevTimeoutEpilogue, tmo)) break;
+      tc_fence_after();
+      uint32_t v[Cfg::kChunks][32];
+#pragma unroll
+      for (int c = 0; c < Cfg::kChunks; ++c)
+        tmem_ld_32x32b_x32(tmem_base + lane_addr + as * kBN + half * NC + c * 32, v[c]);
+      tc_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[as]), 0));
+      if (++as == AS) { as = 0; aph ^= 1; }
+      float acc[NC];
+#pragma unroll
+      for (int c = 0; c < Cfg::kChunks; ++c)
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[c * 32 + j] = __uint_as_float(v[c][j]) * p.alpha;
+      if (m < p.M) {
+        if (p.out_mode == kOutWorkspace) {
+          float* dst = p.ws + ((static_cast<long long>(w.ks) * p.batch + w.b) * p.M + m) * static_cast<long long>(p.N);
+#pragma unroll
+          for (int j = 0; j < NC; j += 4)
+            if (col0 + j < p.N)
+              st_global_v4(dst + col0 + j, __float_as_uint(acc[j]), __float_as_uint(acc[j + 1]),
+                           __float_as_uint(acc[j + 2]), __float_as_uint(acc[j + 3]));
+        } else if (Cfg::kOutF32) {
+          float* dst = reinterpret_cast<float*>(p.c) + w.b * p.c_bstride + m * p.ldc;
+          if (p.out_mode == kOutAtomic) {
+#pragma unroll
+            for (int j = 0; j < NC; j += 4)
+              if (col0 + j < p.N) red_add_v4_f32(dst + col0 + j, acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < NC; j += 4)
+              if (col0 + j < p.N)
+                st_global_v4(dst + col0 + j, __float_as_uint(acc[j]), __float_as_uint(acc[j + 1]),
+                             __float_as_uint(acc[j + 2]), __float_as_uint(acc[j + 3]));
+          }
+        } else {
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.c) + w.b * p.c_bstride + m * p.ldc;
+#pragma unroll
+          for (int j = 0; j < NC; j += 8)
+            if (col0 + j < p.N)
+              st_global_v4(dst + col0 + j, pack_bf16x2(acc[j], acc[j + 1]), pack_bf16x2(acc[j + 2], acc[j + 3]),
+                           pack_bf16x2(acc[j + 4], acc[j + 5]), pack_bf16x2(acc[j + 6], acc[j + 7]));
+        }
+      }
+    }
+  }
+
+  // ------------------------------------------------------------ teardown
+  tc_fence_before();
+  cluster_sync_all();  // the leader's MMAs have retired and both epilogues are done
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair<Cfg::kTmemCols>(tmem_base);
+  }
+}
+
+}  // namespace b2g

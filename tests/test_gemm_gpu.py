@@ -337,3 +337,62 @@ def test_bounded_wait_reports_timeout_and_context_survives(dev, oracle):
     torch.cuda.synchronize()
     assert ops.device_status() == 0
     check_out(out, ref, torch.float32)
+
+
+# ------------------------------------------------------------------ single-CTA path at pair-sized shapes
+_SINGLE_CTA_SCRIPT = r'''
+import sys, numpy as np, torch
+sys.path.insert(0, sys.argv[1])
+from oracle import oracle as O
+from gcnasm_b200 import ops
+dev = torch.device("cuda:0")
+for (M, N, K, pre) in ((512, 512, 512, False), (300, 1024, 1024, True)):
+    qa, sa = O.quant_mx(O.normal_rows(1234, 0, M, K)); qb, sb = O.quant_mx(O.normal_rows(5678, 0, N, K))
+    ref = O.gemm_mx(qa, qb, sa, sb, M, N, K, acc_f64=True)
+    b = O.shuffle_weight_16x16(qb, N, K).reshape(N, K) if pre else qb
+    out = ops.mxfp8_gemm(torch.from_numpy(qa).to(dev), torch.from_numpy(b).to(dev),
+                         torch.from_numpy(O.sf_to_tc_layout(sa)).to(dev), torch.from_numpy(O.sf_to_tc_layout(sb)).to(dev),
+                         out_dtype=torch.bfloat16, b_preshuffled=pre)
+    torch.cuda.synchronize()
+    r = O.check_bf16(out.float().cpu().numpy(), ref)
+    assert r <= 1.0, (M, N, K, pre, r)
+print("single-cta ok")
+'''
+
+
+def test_single_cta_path_when_pairs_disabled(dev):
+    """B2G_DISABLE_PAIR=1 routes M > 128 shapes to the single-CTA 128x256 kernel."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, B2G_DISABLE_PAIR="1")
+    r = subprocess.run([sys.executable, "-c", _SINGLE_CTA_SCRIPT, root], env=env, capture_output=True, text=True,
+                       timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "single-cta ok" in r.stdout
+
+
+def test_bounded_wait_pair_kernel(dev, oracle):
+    """The stall hook on the CTA-pair kernel: the leader's MMA wait gives up, both
+    CTAs retire through their bounded waits, and the context stays usable."""
+    from gcnasm_b200 import capi, ops
+    L = capi.lib()
+    M, N, K = 512, 512, 256
+    qa, sa, qb, sb = mx_operands(oracle, M, N, K)
+    args = (T(qa, dev), T(qb, dev), T(oracle.sf_to_tc_layout(sa), dev), T(oracle.sf_to_tc_layout(sb), dev))
+    assert ops.device_status(clear=True) == 0
+    L.b2g_set_wait_timeout_ms(200)
+    L.b2g_debug_force_stall(1)
+    try:
+        ops.mxfp8_gemm(*args, out_dtype=torch.float32)
+        st = C.c_int(0)
+        assert L.b2g_device_status(C.byref(st), 1) == capi.B2G_ERR_DEVICE_TIMEOUT and st.value != 0
+    finally:
+        L.b2g_debug_force_stall(0)
+        L.b2g_set_wait_timeout_ms(4000)
+    ref = oracle.gemm_mx(qa, qb, sa, sb, M, N, K, acc_f64=True)
+    out = ops.mxfp8_gemm(*args, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    check_out(out, ref, torch.float32)
