@@ -188,14 +188,15 @@ struct TileCfg {
 };
 // Same columns as the reference manifest f4gemm_bf16_per1x32Fp4.csv
 // (tile_M, tile_N, splitK, bpreshuffle, knl_name), one row per kernel variant.
-// tile_M = 256 rows are the CTA-pair kernel (two SMs per tile).
+// tile_M = 256 rows are the CTA-pair kernel (two SMs per tile; 256 x 224 for
+// MXFP8, 256 x 256 for the unscaled fp8 mode).
 const TileCfg kManifest[] = {
     {128, 256, 1, 0, "b2g_sm100a_fp8_128x256"},
     {128, 128, 1, 0, "b2g_sm100a_fp8_128x128"},
     {128, 256, 1, 1, "b2g_sm100a_fp8_128x256_bpreshuffle"},
     {128, 128, 1, 1, "b2g_sm100a_fp8_128x128_bpreshuffle"},
-    {256, 256, 1, 0, "b2g_sm100a_fp8_pair_256x256"},
-    {256, 256, 1, 1, "b2g_sm100a_fp8_pair_256x256_bpreshuffle"},
+    {256, 224, 1, 0, "b2g_sm100a_fp8_pair_256x224"},
+    {256, 224, 1, 1, "b2g_sm100a_fp8_pair_256x224_bpreshuffle"},
 };
 constexpr int kManifestN = sizeof(kManifest) / sizeof(kManifest[0]);
 
@@ -337,18 +338,21 @@ int launch_pair(const Env& d, const CUtensorMap& ta, const CUtensorMap& tb, cons
   return B2G_OK;
 }
 
+// Pair tile width per mode: MX needs 224 so two accumulators + scales fit TMEM.
+constexpr int pair_bn(int mode) { return mode == kModeMX ? 224 : 256; }
+
 int dispatch_pair(const Env& d, int mode, bool pre, bool f32, const CUtensorMap& ta, const CUtensorMap& tb,
                   const CUtensorMap& tsa, const CUtensorMap& tsb, const PairParams& pp, cudaStream_t st) {
   if (mode == kModeMX) {
-    if (pre) return f32 ? launch_pair<PairCfg<kModeMX, true, true>>(d, ta, tb, tsa, tsb, pp, st)
-                        : launch_pair<PairCfg<kModeMX, true, false>>(d, ta, tb, tsa, tsb, pp, st);
-    return f32 ? launch_pair<PairCfg<kModeMX, false, true>>(d, ta, tb, tsa, tsb, pp, st)
-               : launch_pair<PairCfg<kModeMX, false, false>>(d, ta, tb, tsa, tsb, pp, st);
+    if (pre) return f32 ? launch_pair<PairCfg<kModeMX, 224, true, true>>(d, ta, tb, tsa, tsb, pp, st)
+                        : launch_pair<PairCfg<kModeMX, 224, true, false>>(d, ta, tb, tsa, tsb, pp, st);
+    return f32 ? launch_pair<PairCfg<kModeMX, 224, false, true>>(d, ta, tb, tsa, tsb, pp, st)
+               : launch_pair<PairCfg<kModeMX, 224, false, false>>(d, ta, tb, tsa, tsb, pp, st);
   }
-  if (pre) return f32 ? launch_pair<PairCfg<kModePlain, true, true>>(d, ta, tb, tsa, tsb, pp, st)
-                      : launch_pair<PairCfg<kModePlain, true, false>>(d, ta, tb, tsa, tsb, pp, st);
-  return f32 ? launch_pair<PairCfg<kModePlain, false, true>>(d, ta, tb, tsa, tsb, pp, st)
-             : launch_pair<PairCfg<kModePlain, false, false>>(d, ta, tb, tsa, tsb, pp, st);
+  if (pre) return f32 ? launch_pair<PairCfg<kModePlain, 256, true, true>>(d, ta, tb, tsa, tsb, pp, st)
+                      : launch_pair<PairCfg<kModePlain, 256, true, false>>(d, ta, tb, tsa, tsb, pp, st);
+  return f32 ? launch_pair<PairCfg<kModePlain, 256, false, true>>(d, ta, tb, tsa, tsb, pp, st)
+             : launch_pair<PairCfg<kModePlain, 256, false, false>>(d, ta, tb, tsa, tsb, pp, st);
 }
 
 int maybe_sync_check() {
@@ -448,6 +452,7 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
   rc = plan_tiles(r, d.sms, &bn, &S, &kb_per, &bm);
   if (rc) return rc;
   const bool pair = bm == 256;
+  if (pair) bn = pair_bn(r.mode);
   const int KB = cdiv(r.K, 128);
 
   GemmParams p;
@@ -490,7 +495,7 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
   if (!r.bpre) {
     cuuint64_t dims[3] = {(cuuint64_t)r.K, (cuuint64_t)r.N, (cuuint64_t)r.batch};
     cuuint64_t str[2] = {(cuuint64_t)r.ldb, (cuuint64_t)(r.batch > 1 ? r.b_bstride : r.ldb * r.N)};
-    cuuint32_t box[3] = {128, (cuuint32_t)(pair ? 128 : bn), 1};  // a pair CTA loads 128 of the 256 B rows
+    cuuint32_t box[3] = {128, (cuuint32_t)(pair ? bn / 2 : bn), 1};  // a pair CTA loads half the B rows
     rc = encode(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, r.b, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   } else {
@@ -499,7 +504,7 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
     // K-major operand layout of tcgen05.mma, with 256 contiguous bytes per request.
     cuuint64_t dims[4] = {256, (cuuint64_t)(r.N / 16), (cuuint64_t)(r.K / 16), (cuuint64_t)r.batch};
     cuuint64_t str[3] = {(cuuint64_t)16 * r.K, 256, (cuuint64_t)(r.batch > 1 ? r.b_bstride : (long long)r.N * r.K)};
-    cuuint32_t box[4] = {256, (cuuint32_t)((pair ? 128 : bn) / 16), 8, 1};
+    cuuint32_t box[4] = {256, (cuuint32_t)((pair ? bn / 2 : bn) / 16), 8, 1};
     rc = encode(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, r.b, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (rc) return rc;
   }
@@ -530,7 +535,7 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
         const long long bstr = which ? r.sfb_bstride : r.sfa_bstride;
         cuuint64_t dims[4] = {128, (cuuint64_t)kb4, (cuuint64_t)rb, (cuuint64_t)r.batch};
         cuuint64_t str[3] = {512, (cuuint64_t)(kb4 * 512), (cuuint64_t)(r.batch > 1 ? bstr : rb * kb4 * 512)};
-        cuuint32_t box[4] = {128, 1, (cuuint32_t)(which ? 2 : 1), 1};
+        cuuint32_t box[4] = {128, 1, (cuuint32_t)(which ? (bn == 256 ? 2 : 3) : 1), 1};
         rc = encode(which ? &tsb : &tsa, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, which ? (const void*)r.sfb : (const void*)r.sfa,
                     dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
         if (rc) return rc;

@@ -1,9 +1,10 @@
 // b2g_gemm_pair.cuh -- CTA-pair (cluster of 2) variant of the persistent FP8 GEMM.
 //
-// Tile 256 x 256 x 128 per pair; tcgen05.mma.cta_group::2 with M = 256: CTA r of
-// the pair holds A rows [r*128, r*128 + 128) and B rows [r*128, r*128 + 128) of
-// the tile in its own shared memory and receives the 128 x 256 accumulator of
-// its A rows in its own TMEM.  Per SM and 128-K block that is 32 KB of operands
+// Tile 256 x BN x 128 per pair (BN = 256, or 224 for MXFP8 so that two
+// accumulators and the scale factors fit the 512 TMEM columns);
+// tcgen05.mma.cta_group::2 with M = 256: CTA r of the pair holds A rows
+// [r*128, r*128 + 128) and B rows [r*BN/2, (r+1)*BN/2) of the tile in its own
+// shared memory and receives the 128 x BN accumulator of its A rows in its own TMEM.  Per SM and 128-K block that is 32 KB of operands
 // for 128 x 256 x 128 MACs, two thirds of the 48 KB the single-CTA 128 x 256
 // tile needs, which lets the ring hold 6 stages.
 //
@@ -25,27 +26,30 @@
 
 namespace b2g {
 
-template <int kMode_, bool kBPre_, bool kOutF32_>
+template <int kMode_, int kBN_, bool kBPre_, bool kOutF32_>
 struct PairCfg {
   static constexpr int kMode = kMode_;
   static constexpr bool kBPre = kBPre_;
   static constexpr bool kOutF32 = kOutF32_;
-  static constexpr int kBN = 256;     // pair tile N (MMA N)
-  static constexpr int kHalf = 128;   // rows of A and of B per CTA
+  static constexpr int kBN = kBN_;        // pair tile N (MMA N): 256, or 224 for MX
+  static constexpr int kHalf = 128;       // rows of A per CTA
+  static constexpr int kHalfB = kBN / 2;  // rows of B per CTA
   static constexpr int kThreads = 320;
   static constexpr int kEpiWarps = 8;
   static constexpr int kColsPerThread = kBN / 2;
-  static constexpr int kChunks = kColsPerThread / 32;
 
   static constexpr int kABytes = kHalf * 128;
-  static constexpr int kBBytes = kHalf * 128;
+  static constexpr int kBBytes = kHalfB * 128;
+  // A 224-wide tile starts 0/32/64/96 rows into a 128-row scale atom, so its B
+  // scales span up to 3 atoms; the MMA's scale address is shifted by the offset.
+  static constexpr int kSfbAtoms = kBN == 256 ? 2 : 3;
   static constexpr int kSfaBytes = kMode == kModeMX ? 512 : 0;
-  static constexpr int kSfbBytes = kMode == kModeMX ? 1024 : 0;  // both B row blocks of the pair tile
+  static constexpr int kSfbBytes = kMode == kModeMX ? 512 * kSfbAtoms : 0;
   static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
   static constexpr int kStages = 6;
   static constexpr uint32_t kTxPerStage = 2u * kStageBytes;  // both CTAs complete on the leader's barrier
 
-  static constexpr int kSfCols = kMode == kModeMX ? 12 : 0;
+  static constexpr int kSfCols = kMode == kModeMX ? 4 + 4 * kSfbAtoms : 0;
   static constexpr int kAccStages = (2 * kBN + kSfCols <= 512) ? 2 : 1;
   static constexpr int kSfaCol = kAccStages * kBN;
   static constexpr int kSfbCol = kSfaCol + 4;
@@ -60,6 +64,8 @@ struct PairCfg {
   static constexpr int kOffCtl = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffCtl + 16 + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
+  static_assert(kBBytes % 1024 == 0, "B stage must keep 1024-byte swizzle atoms aligned");
+  static_assert(kBN % 32 == 0 && kColsPerThread % 16 == 0, "tile N");
 };
 
 struct PairParams {
@@ -124,7 +130,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       for (int u = pair; u < p.num_units && ok; u += pp.num_pairs) {
         const Unit w = decode_unit(u, p);
         const int arow = w.mt * 256 + static_cast<int>(rank) * 128;  // this CTA's A rows
-        const int brow = w.nt * kBN + static_cast<int>(rank) * 128;  // this CTA's B rows
+        const int brow = w.nt * kBN + static_cast<int>(rank) * Cfg::kHalfB;  // this CTA's B rows
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, kDevTimeoutProducer, tmo)) { ok = false; break; }
           const uint32_t bar = mapa_shared(smem_u32(&full[s]), 0);
@@ -137,7 +143,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
           if (kMode == kModeMX) {
             // scale atoms: (128 words, k-block, row block) boxes of the atom-layout buffers
             tma_load_4d_pair(smem + Cfg::kOffSfa + s * Cfg::kSfaBytes, &tm_sfa, bar, 0, kb, w.mt * 2 + rank, w.b);
-            tma_load_4d_pair(smem + Cfg::kOffSfb + s * Cfg::kSfbBytes, &tm_sfb, bar, 0, kb, w.nt * 2, w.b);
+            tma_load_4d_pair(smem + Cfg::kOffSfb + s * Cfg::kSfbBytes, &tm_sfb, bar, 0, kb, (w.nt * kBN) >> 7, w.b);
           }
           issued_mask |= 1u << s;
           issued_phase = (issued_phase & ~(1u << s)) | (ph << s);
@@ -179,20 +185,22 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
           if (kMode == kModeMX) {
             tc_cp_32x128b_warpx4_pair(tmem_base + Cfg::kSfaCol,
                                       desc_sf_atom(smem_u32(smem + Cfg::kOffSfa + s * Cfg::kSfaBytes)));
-            tc_cp_32x128b_warpx4_pair(tmem_base + Cfg::kSfbCol,
-                                      desc_sf_atom(smem_u32(smem + Cfg::kOffSfb + s * Cfg::kSfbBytes)));
-            tc_cp_32x128b_warpx4_pair(tmem_base + Cfg::kSfbCol + 4,
-                                      desc_sf_atom(smem_u32(smem + Cfg::kOffSfb + s * Cfg::kSfbBytes + 512)));
+#pragma unroll
+            for (int j = 0; j < Cfg::kSfbAtoms; ++j)
+              tc_cp_32x128b_warpx4_pair(tmem_base + Cfg::kSfbCol + 4 * j,
+                                        desc_sf_atom(smem_u32(smem + Cfg::kOffSfb + s * Cfg::kSfbBytes + j * 512)));
           }
+          // B scales of tile row 0 sit ((nt * BN) % 128) / 32 TMEM columns into the first atom
+          const uint32_t sfb_tmem = tmem_base + Cfg::kSfbCol + (((w.nt * kBN) & 127) >> 5);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint64_t adesc = desc_kmajor_sw128(a_base + kk * 32);
-            const uint64_t bdesc = Cfg::kBPre ? desc_kmajor_interleave(b_base + kk * 2 * (Cfg::kHalf * 16), Cfg::kHalf * 16)
+            const uint64_t bdesc = Cfg::kBPre ? desc_kmajor_interleave(b_base + kk * 2 * (Cfg::kHalfB * 16), Cfg::kHalfB * 16)
                                               : desc_kmajor_sw128(b_base + kk * 32);
             const uint32_t acc = (kb > w.kb0 || kk > 0);
             if (kMode == kModeMX)
               mma_mxf8f6f4_pair(d_tmem, adesc, bdesc, idesc_mxf8f6f4(256, kBN, kk, kk), tmem_base + Cfg::kSfaCol,
-                                tmem_base + Cfg::kSfbCol, acc);
+                                sfb_tmem, acc);
             else
               mma_f8f6f4_pair(d_tmem, adesc, bdesc, idesc_f8f6f4(256, kBN), acc);
           }
@@ -224,10 +232,15 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       const int col0 = w.nt * kBN + half * NC;
       if (!mbar_wait(&acc_full[as], aph, abort_flag, p.status, kDevTimeoutEpilogue, tmo)) break;
       tc_fence_after();
-      uint32_t v[Cfg::kChunks][32];
+      constexpr int C32 = NC / 32;
+      uint32_t v[C32 * 32 + 16];
 #pragma unroll
-      for (int c = 0; c < Cfg::kChunks; ++c)
-        tmem_ld_32x32b_x32(tmem_base + lane_addr + as * kBN + half * NC + c * 32, v[c]);
+      for (int c = 0; c < C32; ++c)
+        tmem_ld_32x32b_x32(tmem_base + lane_addr + as * kBN + half * NC + c * 32,
+                           *reinterpret_cast<uint32_t(*)[32]>(&v[c * 32]));
+      if (NC % 32)
+        tmem_ld_32x32b_x16(tmem_base + lane_addr + as * kBN + half * NC + C32 * 32,
+                           *reinterpret_cast<uint32_t(*)[16]>(&v[C32 * 32]));
       tc_wait_ld();
       tc_fence_before();
       __syncwarp();
@@ -235,9 +248,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       if (++as == AS) { as = 0; aph ^= 1; }
       float acc[NC];
 #pragma unroll
-      for (int c = 0; c < Cfg::kChunks; ++c)
-#pragma unroll
-        for (int j = 0; j < 32; ++j) acc[c * 32 + j] = __uint_as_float(v[c][j]) * p.alpha;
+      for (int j = 0; j < NC; ++j) acc[j] = __uint_as_float(v[j]) * p.alpha;
       if (m < p.M) {
         if (p.out_mode == kOutWorkspace) {
           float* dst = p.ws + ((static_cast<long long>(w.ks) * p.batch + w.b) * p.M + m) * static_cast<long long>(p.N);
