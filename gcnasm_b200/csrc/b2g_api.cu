@@ -204,7 +204,7 @@ constexpr int kManifestN = sizeof(kManifest) / sizeof(kManifest[0]);
 // ceil(tiles * splitK / num_sm); ties go to fewer idle SMs, then to the larger
 // tile_m*tile_n/(tile_m+tile_n); manifest order breaks remaining ties.
 void select_tile(int M, int N, int num_sm, int log2_k_split, int bpreshuffle, int* idx, int* log2_out,
-                 int max_tile_n = 1 << 30) {
+                 int max_tile_n = 1 << 30, int max_tile_m = 1 << 30) {
   uint32_t empty_cu = static_cast<uint32_t>(num_sm);
   uint32_t round = 0xffffffffu;
   float effi = 1.0f;
@@ -213,7 +213,7 @@ void select_tile(int M, int N, int num_sm, int log2_k_split, int bpreshuffle, in
   int sel = -1, sel_split = 1;
   for (int i = 0; i < kManifestN; ++i) {
     const TileCfg& c = kManifest[i];
-    if (c.bpre != bpre_en || c.splitk < split_en || c.tile_n > max_tile_n) continue;
+    if (c.bpre != bpre_en || c.splitk < split_en || c.tile_n > max_tile_n || c.tile_m > max_tile_m) continue;
     if (c.tile_m == 128 && c.tile_n == 512 && (N % c.tile_n) != 0) continue;
     int cand[4], nc = 0;
     if (log2_k_split >= 0 && c.splitk) cand[nc++] = 1 << log2_k_split;
@@ -312,6 +312,7 @@ int dispatch_bn(const Env& d, int bn, bool pre, bool f32, const CUtensorMap& ta,
   // The blockwise mode keeps 128 fp32 sums per epilogue thread at kBN = 256,
   // more than the 168-register budget of a 10-warp CTA; it runs 128-wide tiles.
   if (kMode != kModeBlk && bn == 256) return dispatch_pre_out<kMode, 256>(d, pre, f32, ta, tb, p, grid, st);
+  if (bn != 128) return fail(B2G_ERR_UNSUPPORTED, "no single-CTA kernel of width %d", bn);
   return dispatch_pre_out<kMode, 128>(d, pre, f32, ta, tb, p, grid, st);
 }
 
@@ -338,11 +339,9 @@ int launch_pair(const Env& d, const CUtensorMap& ta, const CUtensorMap& tb, cons
   return B2G_OK;
 }
 
-// Pair tile width per mode: MX needs 224 so two accumulators + scales fit TMEM.
-constexpr int pair_bn(int mode) { return mode == kModeMX ? 224 : 256; }
-
-int dispatch_pair(const Env& d, int mode, bool pre, bool f32, const CUtensorMap& ta, const CUtensorMap& tb,
+int dispatch_pair(const Env& d, int mode, int bn, bool pre, bool f32, const CUtensorMap& ta, const CUtensorMap& tb,
                   const CUtensorMap& tsa, const CUtensorMap& tsb, const PairParams& pp, cudaStream_t st) {
+  if (bn != (mode == kModeMX ? 224 : 256)) return fail(B2G_ERR_UNSUPPORTED, "no pair kernel of width %d", bn);
   if (mode == kModeMX) {
     if (pre) return f32 ? launch_pair<PairCfg<kModeMX, 224, true, true>>(d, ta, tb, tsa, tsb, pp, st)
                         : launch_pair<PairCfg<kModeMX, 224, true, false>>(d, ta, tb, tsa, tsb, pp, st);
@@ -373,20 +372,24 @@ int plan_tiles(const Req& r, int sms, int* bn_out, int* S_out, int* kb_per_out, 
   int bn = r.bn, l2 = r.log2_k_split, bm = 128;
   if (r.mode == kModeBlk && bn == 256) bn = 128;
   if (bn == 0) {
+    // The pair tile wastes half its rows at M <= 128 and the blockwise mode has no
+    // pair kernel: those select among the single-CTA entries only.
+    static const bool pair_off = [] {
+      const char* v = getenv("B2G_DISABLE_PAIR");
+      return v && v[0] == '1';
+    }();
+    const bool pair_ok = r.M > 128 && r.mode != kModeBlk && !pair_off;
     int idx = -1, lsel = 0;
-    select_tile(r.M, r.N, sms, r.log2_k_split, r.bpre ? 1 : 0, &idx, &lsel, r.mode == kModeBlk ? 128 : 1 << 30);
+    select_tile(r.M, r.N, sms, r.log2_k_split, r.bpre ? 1 : 0, &idx, &lsel, r.mode == kModeBlk ? 128 : 1 << 30,
+                pair_ok ? 1 << 30 : 128);
     if (idx < 0) return fail(B2G_ERR_UNSUPPORTED, "no tile in the manifest fits");
     bn = kManifest[idx].tile_n;
     bm = kManifest[idx].tile_m;
     l2 = lsel;
   }
-  // The pair tile wastes half its rows at M <= 128 (and the blockwise mode has no
-  // pair kernel): those run the single-CTA 128 x 256 tile.
-  static const bool pair_off = [] {
-    const char* v = getenv("B2G_DISABLE_PAIR");
-    return v && v[0] == '1';
-  }();
-  if (bm == 256 && (r.M <= 128 || r.mode == kModeBlk || pair_off)) bm = 128;
+  // the widths the kernels are compiled for: pair 224 (MX) / 256, single CTA 256 / 128
+  if (bm == 256) bn = r.mode == kModeMX ? 224 : 256;
+  else bn = (r.mode != kModeBlk && bn == 256) ? 256 : 128;
   if (bm_out) *bm_out = bm;
   if (l2 < 0) l2 = 0;
   if (l2 > 8) return fail(B2G_ERR_INVALID_ARG, "log2_k_split %d too large", l2);
@@ -452,7 +455,6 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
   rc = plan_tiles(r, d.sms, &bn, &S, &kb_per, &bm);
   if (rc) return rc;
   const bool pair = bm == 256;
-  if (pair) bn = pair_bn(r.mode);
   const int KB = cdiv(r.K, 128);
 
   GemmParams p;
@@ -544,7 +546,7 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
     PairParams pp;
     pp.g = p;
     pp.num_pairs = static_cast<int>(std::min<long long>(units, d.sms / 2));
-    rc = dispatch_pair(d, r.mode, r.bpre, r.out_f32, ta, tb, tsa, tsb, pp, r.stream);
+    rc = dispatch_pair(d, r.mode, bn, r.bpre, r.out_f32, ta, tb, tsa, tsb, pp, r.stream);
     if (rc) return rc;
   } else {
   const int grid = static_cast<int>(std::min<long long>(units, d.sms));
