@@ -1,12 +1,13 @@
 // b2g_gemm_pair.cuh -- CTA-pair (cluster of 2) variant of the persistent FP8 GEMM.
 //
-// Tile 256 x BN x 128 per pair (BN = 256, or 224 for MXFP8 so that two
+// Tile 256 x BN x 128 per pair (BN = 256, or 192 for MXFP8 so that two
 // accumulators and the scale factors fit the 512 TMEM columns);
 // tcgen05.mma.cta_group::2 with M = 256: CTA r of the pair holds A rows
 // [r*128, r*128 + 128) and B rows [r*BN/2, (r+1)*BN/2) of the tile in its own
-// shared memory and receives the 128 x BN accumulator of its A rows in its own TMEM.  Per SM and 128-K block that is 32 KB of operands
-// for 128 x 256 x 128 MACs, two thirds of the 48 KB the single-CTA 128 x 256
-// tile needs, which lets the ring hold 6 stages.
+// shared memory and receives the 128 x BN accumulator of its A rows in its own
+// TMEM.  At BN = 256 that is 32 KB of operands per SM and 128-K block for
+// 128 x 256 x 128 MACs, two thirds of the 48 KB the single-CTA 128 x 256 tile
+// needs, which lets the ring hold 6 stages.
 //
 // Protocol (leader = cluster rank 0):
 //   * both CTAs allocate TMEM with cta_group::2 and free it after a cluster sync;
@@ -31,7 +32,7 @@ struct PairCfg {
   static constexpr int kMode = kMode_;
   static constexpr bool kBPre = kBPre_;
   static constexpr bool kOutF32 = kOutF32_;
-  static constexpr int kBN = kBN_;        // pair tile N (MMA N): 256, or 224 for MX
+  static constexpr int kBN = kBN_;        // pair tile N (MMA N): 256, or 192 for MX
   static constexpr int kHalf = 128;       // rows of A per CTA
   static constexpr int kHalfB = kBN / 2;  // rows of B per CTA
   static constexpr int kThreads = 320;
@@ -40,9 +41,10 @@ struct PairCfg {
 
   static constexpr int kABytes = kHalf * 128;
   static constexpr int kBBytes = kHalfB * 128;
-  // A 224-wide tile starts 0/32/64/96 rows into a 128-row scale atom, so its B
-  // scales span up to 3 atoms; the MMA's scale address is shifted by the offset.
-  static constexpr int kSfbAtoms = kBN == 256 ? 2 : 3;
+  // A 192-wide tile starts 0 or 64 rows into a 128-row scale atom, so its B
+  // scales span 2 atoms and the MMA's scale address is shifted by 0 or 2 TMEM
+  // columns (the even shift CUTLASS's N=192 tiles use).
+  static constexpr int kSfbAtoms = 2;
   static constexpr int kSfaBytes = kMode == kModeMX ? 512 : 0;
   static constexpr int kSfbBytes = kMode == kModeMX ? 512 * kSfbAtoms : 0;
   static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
@@ -65,7 +67,9 @@ struct PairCfg {
   static constexpr int kSmemBytes = kOffCtl + 16 + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   static_assert(kBBytes % 1024 == 0, "B stage must keep 1024-byte swizzle atoms aligned");
-  static_assert(kBN % 32 == 0 && kColsPerThread % 16 == 0, "tile N");
+  // every TMEM column address the kernel forms is a multiple of 32 (loads,
+  // accumulator stages) and scale shifts stay even
+  static_assert(kBN % 64 == 0 && kColsPerThread % 32 == 0, "tile N");
 };
 
 struct PairParams {
@@ -233,14 +237,11 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       if (!mbar_wait(&acc_full[as], aph, abort_flag, p.status, kDevTimeoutEpilogue, tmo)) break;
       tc_fence_after();
       constexpr int C32 = NC / 32;
-      uint32_t v[C32 * 32 + 16];
+      uint32_t v[NC];
 #pragma unroll
       for (int c = 0; c < C32; ++c)
         tmem_ld_32x32b_x32(tmem_base + lane_addr + as * kBN + half * NC + c * 32,
                            *reinterpret_cast<uint32_t(*)[32]>(&v[c * 32]));
-      if (NC % 32)
-        tmem_ld_32x32b_x16(tmem_base + lane_addr + as * kBN + half * NC + C32 * 32,
-                           *reinterpret_cast<uint32_t(*)[16]>(&v[C32 * 32]));
       tc_wait_ld();
       tc_fence_before();
       __syncwarp();
