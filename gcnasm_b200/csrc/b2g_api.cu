@@ -188,15 +188,14 @@ struct TileCfg {
 };
 // Same columns as the reference manifest f4gemm_bf16_per1x32Fp4.csv
 // (tile_M, tile_N, splitK, bpreshuffle, knl_name), one row per kernel variant.
-// tile_M = 256 rows are the CTA-pair kernel (two SMs per tile; 256 x 192 for
-// MXFP8, 256 x 256 for the unscaled fp8 mode).
+// tile_M = 256 rows are the CTA-pair kernel (two SMs per tile).
 const TileCfg kManifest[] = {
     {128, 256, 1, 0, "b2g_sm100a_fp8_128x256"},
     {128, 128, 1, 0, "b2g_sm100a_fp8_128x128"},
     {128, 256, 1, 1, "b2g_sm100a_fp8_128x256_bpreshuffle"},
     {128, 128, 1, 1, "b2g_sm100a_fp8_128x128_bpreshuffle"},
-    {256, 192, 1, 0, "b2g_sm100a_fp8_pair_256x192"},
-    {256, 192, 1, 1, "b2g_sm100a_fp8_pair_256x192_bpreshuffle"},
+    {256, 256, 1, 0, "b2g_sm100a_fp8_pair_256x256"},
+    {256, 256, 1, 1, "b2g_sm100a_fp8_pair_256x256_bpreshuffle"},
 };
 constexpr int kManifestN = sizeof(kManifest) / sizeof(kManifest[0]);
 
@@ -341,12 +340,12 @@ int launch_pair(const Env& d, const CUtensorMap& ta, const CUtensorMap& tb, cons
 
 int dispatch_pair(const Env& d, int mode, int bn, bool pre, bool f32, const CUtensorMap& ta, const CUtensorMap& tb,
                   const CUtensorMap& tsa, const CUtensorMap& tsb, const PairParams& pp, cudaStream_t st) {
-  if (bn != (mode == kModeMX ? 192 : 256)) return fail(B2G_ERR_UNSUPPORTED, "no pair kernel of width %d", bn);
+  if (bn != 256) return fail(B2G_ERR_UNSUPPORTED, "no pair kernel of width %d", bn);
   if (mode == kModeMX) {
-    if (pre) return f32 ? launch_pair<PairCfg<kModeMX, 192, true, true>>(d, ta, tb, tsa, tsb, pp, st)
-                        : launch_pair<PairCfg<kModeMX, 192, true, false>>(d, ta, tb, tsa, tsb, pp, st);
-    return f32 ? launch_pair<PairCfg<kModeMX, 192, false, true>>(d, ta, tb, tsa, tsb, pp, st)
-               : launch_pair<PairCfg<kModeMX, 192, false, false>>(d, ta, tb, tsa, tsb, pp, st);
+    if (pre) return f32 ? launch_pair<PairCfg<kModeMX, 256, true, true>>(d, ta, tb, tsa, tsb, pp, st)
+                        : launch_pair<PairCfg<kModeMX, 256, true, false>>(d, ta, tb, tsa, tsb, pp, st);
+    return f32 ? launch_pair<PairCfg<kModeMX, 256, false, true>>(d, ta, tb, tsa, tsb, pp, st)
+               : launch_pair<PairCfg<kModeMX, 256, false, false>>(d, ta, tb, tsa, tsb, pp, st);
   }
   if (pre) return f32 ? launch_pair<PairCfg<kModePlain, 256, true, true>>(d, ta, tb, tsa, tsb, pp, st)
                       : launch_pair<PairCfg<kModePlain, 256, true, false>>(d, ta, tb, tsa, tsb, pp, st);
@@ -387,8 +386,8 @@ int plan_tiles(const Req& r, int sms, int* bn_out, int* S_out, int* kb_per_out, 
     bm = kManifest[idx].tile_m;
     l2 = lsel;
   }
-  // the widths the kernels are compiled for: pair 192 (MX) / 256, single CTA 256 / 128
-  if (bm == 256) bn = r.mode == kModeMX ? 192 : 256;
+  // the widths the kernels are compiled for: pair 256, single CTA 256 / 128
+  if (bm == 256) bn = 256;
   else bn = (r.mode != kModeBlk && bn == 256) ? 256 : 128;
   if (bm_out) *bm_out = bm;
   if (l2 < 0) l2 = 0;

@@ -1,7 +1,7 @@
 // b2g_gemm_pair.cuh -- CTA-pair (cluster of 2) variant of the persistent FP8 GEMM.
 //
-// Tile 256 x BN x 128 per pair (BN = 256, or 192 for MXFP8 so that two
-// accumulators and the scale factors fit the 512 TMEM columns);
+// Tile 256 x BN x 128 per pair (BN = 256; 192 also compiles, with a
+// double-buffered MX accumulator, but measured slower at 8192^3);
 // tcgen05.mma.cta_group::2 with M = 256: CTA r of the pair holds A rows
 // [r*128, r*128 + 128) and B rows [r*BN/2, (r+1)*BN/2) of the tile in its own
 // shared memory and receives the 128 x BN accumulator of its A rows in its own
@@ -32,7 +32,7 @@ struct PairCfg {
   static constexpr int kMode = kMode_;
   static constexpr bool kBPre = kBPre_;
   static constexpr bool kOutF32 = kOutF32_;
-  static constexpr int kBN = kBN_;        // pair tile N (MMA N): 256, or 192 for MX
+  static constexpr int kBN = kBN_;        // pair tile N (MMA N): 256 or 192
   static constexpr int kHalf = 128;       // rows of A per CTA
   static constexpr int kHalfB = kBN / 2;  // rows of B per CTA
   static constexpr int kThreads = 320;

@@ -32,7 +32,7 @@ SYNTH_MANIFEST = np.array([
     [32, 128, 1, 1], [256, 128, 1, 1], [160, 384, 0, 1], [256, 256, 0, 0],
 ], dtype=np.int32)
 LIB_MANIFEST = np.array([[128, 256, 1, 0], [128, 128, 1, 0], [128, 256, 1, 1], [128, 128, 1, 1],
-                        [256, 192, 1, 0], [256, 192, 1, 1]], dtype=np.int32)
+                        [256, 256, 1, 0], [256, 256, 1, 1]], dtype=np.int32)
 
 # asm_f4gemm/run_tests.sh:363-367 heuristic shapes, the split-K sweep shape and
 # the benchmark configs' shapes
