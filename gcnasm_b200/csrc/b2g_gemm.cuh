@@ -111,10 +111,13 @@ struct GemmCfg {
   static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
   static constexpr int kStages = (kBN == 256) ? 4 : 6;
 
-  // TMEM: accumulator (or per-K-block partial) buffers, then the MX scales
+  // TMEM: accumulator (or per-K-block partial) buffers, then the MX scales in two
+  // alternating column sets (the copies for block k+1 never overwrite columns the
+  // MMAs of block k still read)
   static constexpr int kSfCols = kMode == kModeMX ? 4 + 4 * kSfbAtoms : 0;
-  static constexpr int kAccStages = (kMode == kModeBlk) ? 2 : ((2 * kBN + kSfCols <= 512) ? 2 : 1);
-  static constexpr int kSfaCol = kAccStages * kBN;
+  static constexpr int kSfBufs = 2;
+  static constexpr int kAccStages = (kMode == kModeBlk) ? 2 : ((2 * kBN + kSfBufs * kSfCols <= 512) ? 2 : 1);
+  static constexpr int kSfaCol = kAccStages * kBN;  // + buffer * kSfCols
   static constexpr int kSfbCol = kSfaCol + 4;
   static constexpr int kTmemCols = 512;
 
@@ -229,7 +232,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       int s = 0, as = 0;
-      uint32_t ph = 0, aph = 0;
+      uint32_t ph = 0, aph = 0, sfbuf = 0;
       bool ok = true;
       if (p.debug_stall) ok = mbar_wait(never, 0, abort_flag, p.status, kDevTimeoutMma, tmo);
       for (int u = blockIdx.x; u < p.num_units && ok; u += gridDim.x) {
@@ -247,11 +250,14 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
           const uint32_t a_base = smem_u32(smem + Cfg::kOffA + s * Cfg::kABytes);
           const uint32_t b_base = smem_u32(smem + Cfg::kOffB + s * Cfg::kBBytes);
           const uint32_t d_tmem = tmem_base + as * kBN;
+          const uint32_t sf_off = sfbuf * Cfg::kSfCols;
+          sfbuf ^= 1;
           if (kMode == kModeMX) {
-            tc_cp_32x128b_warpx4(tmem_base + Cfg::kSfaCol, desc_sf_atom(smem_u32(smem + Cfg::kOffSfa + s * Cfg::kSfaBytes)));
+            tc_cp_32x128b_warpx4(tmem_base + Cfg::kSfaCol + sf_off,
+                                 desc_sf_atom(smem_u32(smem + Cfg::kOffSfa + s * Cfg::kSfaBytes)));
 #pragma unroll
             for (int j = 0; j < Cfg::kSfbAtoms; ++j)
-              tc_cp_32x128b_warpx4(tmem_base + Cfg::kSfbCol + 4 * j,
+              tc_cp_32x128b_warpx4(tmem_base + Cfg::kSfbCol + sf_off + 4 * j,
                                    desc_sf_atom(smem_u32(smem + Cfg::kOffSfb + s * Cfg::kSfbBytes + j * 512)));
           }
 #pragma unroll
@@ -261,8 +267,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                                               : desc_kmajor_sw128(b_base + kk * 32);
             const uint32_t acc = (kMode == kModeBlk) ? (kk > 0) : (kb > w.kb0 || kk > 0);
             if (kMode == kModeMX)
-              mma_mxf8f6f4(d_tmem, adesc, bdesc, idesc_mxf8f6f4(128, kBN, kk, kk), tmem_base + Cfg::kSfaCol,
-                           tmem_base + Cfg::kSfbCol, acc);
+              mma_mxf8f6f4(d_tmem, adesc, bdesc, idesc_mxf8f6f4(128, kBN, kk, kk), tmem_base + Cfg::kSfaCol + sf_off,
+                           tmem_base + Cfg::kSfbCol + sf_off, acc);
             else
               mma_f8f6f4(d_tmem, adesc, bdesc, idesc_f8f6f4(128, kBN), acc);
           }

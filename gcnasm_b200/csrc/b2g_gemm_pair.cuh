@@ -51,9 +51,12 @@ struct PairCfg {
   static constexpr int kStages = 6;
   static constexpr uint32_t kTxPerStage = 2u * kStageBytes;  // both CTAs complete on the leader's barrier
 
+  // Scale factors live in TMEM in two alternating column sets: the copies for
+  // 128-K block k+1 then never overwrite columns the MMAs of block k still read.
   static constexpr int kSfCols = kMode == kModeMX ? 4 + 4 * kSfbAtoms : 0;
-  static constexpr int kAccStages = (2 * kBN + kSfCols <= 512) ? 2 : 1;
-  static constexpr int kSfaCol = kAccStages * kBN;
+  static constexpr int kSfBufs = 2;
+  static constexpr int kAccStages = (2 * kBN + kSfBufs * kSfCols <= 512) ? 2 : 1;
+  static constexpr int kSfaCol = kAccStages * kBN;  // + buffer * kSfCols
   static constexpr int kSfbCol = kSfaCol + 4;
   static constexpr int kTmemCols = 512;
 
@@ -172,7 +175,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     // ------------------------------------------------------------ MMA issuer (leader only)
     if (leader && lane == 0) {
       int s = 0, as = 0;
-      uint32_t ph = 0, aph = 0;
+      uint32_t ph = 0, aph = 0, sfbuf = 0;
       bool ok = true;
       constexpr uint16_t kBoth = 0x3;
       if (p.debug_stall) ok = mbar_wait(never, 0, abort_flag, p.status, kDevTimeoutMma, tmo);
@@ -186,16 +189,19 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
           const uint32_t a_base = smem_u32(smem + Cfg::kOffA + s * Cfg::kABytes);
           const uint32_t b_base = smem_u32(smem + Cfg::kOffB + s * Cfg::kBBytes);
           const uint32_t d_tmem = tmem_base + as * kBN;
+          const uint32_t sf_off = sfbuf * Cfg::kSfCols;
           if (kMode == kModeMX) {
-            tc_cp_32x128b_warpx4_pair(tmem_base + Cfg::kSfaCol,
+            tc_cp_32x128b_warpx4_pair(tmem_base + Cfg::kSfaCol + sf_off,
                                       desc_sf_atom(smem_u32(smem + Cfg::kOffSfa + s * Cfg::kSfaBytes)));
 #pragma unroll
             for (int j = 0; j < Cfg::kSfbAtoms; ++j)
-              tc_cp_32x128b_warpx4_pair(tmem_base + Cfg::kSfbCol + 4 * j,
+              tc_cp_32x128b_warpx4_pair(tmem_base + Cfg::kSfbCol + sf_off + 4 * j,
                                         desc_sf_atom(smem_u32(smem + Cfg::kOffSfb + s * Cfg::kSfbBytes + j * 512)));
           }
           // B scales of tile row 0 sit ((nt * BN) % 128) / 32 TMEM columns into the first atom
-          const uint32_t sfb_tmem = tmem_base + Cfg::kSfbCol + (((w.nt * kBN) & 127) >> 5);
+          const uint32_t sfa_tmem = tmem_base + Cfg::kSfaCol + sf_off;
+          const uint32_t sfb_tmem = tmem_base + Cfg::kSfbCol + sf_off + (((w.nt * kBN) & 127) >> 5);
+          sfbuf ^= 1;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint64_t adesc = desc_kmajor_sw128(a_base + kk * 32);
@@ -203,8 +209,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
                                               : desc_kmajor_sw128(b_base + kk * 32);
             const uint32_t acc = (kb > w.kb0 || kk > 0);
             if (kMode == kModeMX)
-              mma_mxf8f6f4_pair(d_tmem, adesc, bdesc, idesc_mxf8f6f4(256, kBN, kk, kk), tmem_base + Cfg::kSfaCol,
-                                sfb_tmem, acc);
+              mma_mxf8f6f4_pair(d_tmem, adesc, bdesc, idesc_mxf8f6f4(256, kBN, kk, kk), sfa_tmem, sfb_tmem, acc);
             else
               mma_f8f6f4_pair(d_tmem, adesc, bdesc, idesc_f8f6f4(256, kBN), acc);
           }
