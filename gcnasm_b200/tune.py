@@ -55,6 +55,50 @@ def make_call(mode, ab, out, log2, group_n=128, bpre=False):
     return lambda: ops.gemm_a8w8(qa, qb, out=out, log2_k_split=log2, b_preshuffled=bpre)
 
 
+class Clocks:
+    """Median SM clock (MHz) and power (W) of GPU 0 while the timed rounds run (NVML)."""
+
+    def __init__(self):
+        self.samples = []
+        self._stop = None
+
+    def __enter__(self):
+        import threading
+        import time
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByIndex(torch.cuda.current_device())
+        except Exception:
+            return self
+        self._stop = threading.Event()
+
+        def loop():
+            while not self._stop.is_set():
+                try:
+                    self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                                         nv.nvmlDeviceGetPowerUsage(h) / 1000.0))
+                except Exception:
+                    pass
+                time.sleep(0.002)
+
+        self._thr = threading.Thread(target=loop, daemon=True)
+        self._thr.start()
+        return self
+
+    def __exit__(self, *a):
+        if self._stop:
+            self._stop.set()
+            self._thr.join(timeout=5)
+
+    def summary(self):
+        if not self.samples:
+            return "clocks n/a"
+        sm = statistics.median(c for c, _ in self.samples)
+        pw = statistics.median(w for _, w in self.samples)
+        return f"sm {sm:.0f} MHz  {pw:.0f} W"
+
+
 def time_rounds(fn, warmup, iters, rounds, flush_bytes=0):
     """Best / median / worst per-call milliseconds over `rounds` rounds of `iters` calls."""
     buf = torch.empty(flush_bytes, dtype=torch.uint8, device="cuda") if flush_bytes else None
@@ -117,7 +161,8 @@ def main(argv=None):
     for l2 in splits:
         fn = make_call(a.mode, ab, out, l2, a.group_n, bool(a.bpreshuffle))
         try:
-            best, med, worst = time_rounds(fn, a.warmup, a.iters, a.rounds, 256 << 20 if a.flush_l2 else 0)
+            with Clocks() as clk:
+                best, med, worst = time_rounds(fn, a.warmup, a.iters, a.rounds, 256 << 20 if a.flush_l2 else 0)
         except capi.B2GError as e:
             print(f"split {l2}: {e}")
             continue
@@ -125,7 +170,7 @@ def main(argv=None):
         gb = lambda t: nbytes / (t * 1e-3) / 1e9  # noqa: E731
         print(f"[{a.mode} M={M} N={N} K={K} out={a.out} log2_split={l2} bpre={a.bpreshuffle}] "
               f"best={best * 1e3:.2f} us  median={med * 1e3:.2f} us  worst={worst * 1e3:.2f} us  "
-              f"{tf(best):.1f} TFLOP/s  {gb(best):.1f} GB/s")
+              f"{tf(best):.1f} TFLOP/s  {gb(best):.1f} GB/s  [{clk.summary()}]")
         rows.append([a.mode, M, N, K, a.out, a.bpreshuffle, l2, f"{best * 1e3:.3f}", f"{tf(best):.2f}",
                      f"{gb(best):.1f}"])
     if a.sweep and rows:
