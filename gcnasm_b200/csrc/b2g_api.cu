@@ -22,6 +22,7 @@
 #include "b2g_aux.cuh"
 #include "b2g_gemm.cuh"
 #include "b2g_gemm_pair.cuh"
+#include "b2g_gemm_skinny.cuh"
 
 using namespace b2g;
 
@@ -402,9 +403,110 @@ int plan_tiles(const Req& r, int sms, int* bn_out, int* S_out, int* kb_per_out, 
   return B2G_OK;
 }
 
+// Few rows of A (decode): the transposed stream-K kernel.
+bool use_skinny(const Req& r) {
+  static const bool off = [] {
+    const char* v = getenv("B2G_DISABLE_SKINNY");
+    return v && v[0] == '1';
+  }();
+  return !off && r.M <= 128 && r.batch == 1 && r.mode != kModeBlk;
+}
+
 // Scratch bytes run_gemm will ask for beyond r.ws_offset.
 size_t split_ws_bytes(const Req& r, int S) {
+  if (use_skinny(r)) return r.out_f32 ? 0 : static_cast<size_t>(r.M) * r.N * 4;  // fp32 sums before the cast
   return (S > 1 && !r.out_f32) ? static_cast<size_t>(S) * r.batch * r.M * r.N * 4 : 0;
+}
+
+template <class Cfg>
+int launch_skinny(const Env& d, const CUtensorMap& tw, const CUtensorMap& ta, const SkinnyParams& sp, int grid,
+                  cudaStream_t st) {
+  const void* fn = reinterpret_cast<const void*>(&b2g_gemm_skinny_kernel<Cfg>);
+  int rc = ensure_smem_attr(d.fns, fn, Cfg::kSmemBytes);
+  if (rc) return rc;
+  b2g_gemm_skinny_kernel<Cfg><<<grid, Cfg::kThreads, Cfg::kSmemBytes, st>>>(tw, ta, sp);
+  B2G_CUDA(cudaGetLastError());
+  return B2G_OK;
+}
+
+template <int kMode, bool kPre>
+int dispatch_skinny_mp(const Env& d, int mp, const CUtensorMap& tw, const CUtensorMap& ta, const SkinnyParams& sp,
+                       int grid, cudaStream_t st) {
+  switch (mp) {
+    case 16: return launch_skinny<SkinnyCfg<kMode, 16, kPre>>(d, tw, ta, sp, grid, st);
+    case 32: return launch_skinny<SkinnyCfg<kMode, 32, kPre>>(d, tw, ta, sp, grid, st);
+    case 64: return launch_skinny<SkinnyCfg<kMode, 64, kPre>>(d, tw, ta, sp, grid, st);
+    default: return launch_skinny<SkinnyCfg<kMode, 128, kPre>>(d, tw, ta, sp, grid, st);
+  }
+}
+
+int run_skinny(const Req& r, const Env& d) {
+  int rc = B2G_OK;
+  const int mp = r.M <= 16 ? 16 : r.M <= 32 ? 32 : r.M <= 64 ? 64 : 128;
+  SkinnyParams sp;
+  memset(&sp, 0, sizeof(sp));
+  sp.M = r.M; sp.N = r.N; sp.K = r.K;
+  sp.alpha = r.alpha;
+  sp.sfw = r.sfb;
+  sp.sfa = r.sfa;
+  sp.sf_rb = static_cast<long long>(cdiv(r.K, 128)) * 512;
+  sp.NT = cdiv(r.N, 128);
+  sp.KB = cdiv(r.K, 128);
+  sp.units = static_cast<long long>(sp.NT) * sp.KB;
+  sp.status = d.status;
+  sp.timeout_ns = g_timeout_ns.load();
+  sp.debug_stall = g_force_stall.load();
+
+  CUtensorMap tw, ta;
+  if (!r.bpre) {
+    cuuint64_t dims[3] = {(cuuint64_t)r.K, (cuuint64_t)r.N, 1};
+    cuuint64_t str[2] = {(cuuint64_t)r.ldb, (cuuint64_t)(r.ldb * r.N)};
+    cuuint32_t box[3] = {128, 128, 1};
+    rc = encode(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, r.b, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  } else {
+    cuuint64_t dims[4] = {256, (cuuint64_t)(r.N / 16), (cuuint64_t)(r.K / 16), 1};
+    cuuint64_t str[3] = {(cuuint64_t)16 * r.K, 256, (cuuint64_t)((long long)r.N * r.K)};
+    cuuint32_t box[4] = {256, 8, 8, 1};
+    rc = encode(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, r.b, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+  }
+  if (rc) return rc;
+  {
+    cuuint64_t dims[3] = {(cuuint64_t)r.K, (cuuint64_t)r.M, 1};
+    cuuint64_t str[2] = {(cuuint64_t)r.lda, (cuuint64_t)(r.lda * r.M)};
+    cuuint32_t box[3] = {128, (cuuint32_t)mp, 1};
+    rc = encode(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, r.a, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
+  // partial sums are added into zeroed fp32: C itself, or scratch cast to bf16 afterwards
+  float* acc = nullptr;
+  long long ldacc = 0;
+  if (r.out_f32) {
+    acc = static_cast<float*>(r.c);
+    ldacc = r.ldc;
+  } else {
+    void* ws = nullptr;
+    rc = env_workspace(d, r.ws_offset + static_cast<size_t>(r.M) * r.N * 4, &ws);
+    if (rc) return rc;
+    acc = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + r.ws_offset);
+    ldacc = r.N;
+  }
+  B2G_CUDA(cudaMemset2DAsync(acc, ldacc * 4, 0, static_cast<size_t>(r.N) * 4, r.M, r.stream));
+  sp.c = acc;
+  sp.ldc = ldacc;
+  const int grid = static_cast<int>(std::min<long long>(sp.units, d.sms));
+  if (r.mode == kModeMX)
+    rc = r.bpre ? dispatch_skinny_mp<kModeMX, true>(d, mp, tw, ta, sp, grid, r.stream)
+                : dispatch_skinny_mp<kModeMX, false>(d, mp, tw, ta, sp, grid, r.stream);
+  else
+    rc = r.bpre ? dispatch_skinny_mp<kModePlain, true>(d, mp, tw, ta, sp, grid, r.stream)
+                : dispatch_skinny_mp<kModePlain, false>(d, mp, tw, ta, sp, grid, r.stream);
+  if (rc) return rc;
+  if (!r.out_f32) {
+    const long long work = static_cast<long long>(r.M) * (r.N / 4);
+    b2g_splitk_reduce_kernel<false><<<grid_for(work, 256, d.sms), 256, 0, r.stream>>>(acc, r.c, 1, 1, r.M, r.N, r.ldc, 0);
+    B2G_CUDA(cudaGetLastError());
+  }
+  return maybe_sync_check();
 }
 
 int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
@@ -448,6 +550,7 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
     env = env_of(dst);
   }
   const Env& d = env;
+  if (use_skinny(r)) return run_skinny(r, d);
 
   // ---- tile + split
   int bn = 0, S = 1, kb_per = 1, bm = 128;

@@ -346,7 +346,7 @@ sys.path.insert(0, sys.argv[1])
 from oracle import oracle as O
 from gcnasm_b200 import ops
 dev = torch.device("cuda:0")
-for (M, N, K, pre) in ((512, 512, 512, False), (300, 1024, 1024, True)):
+for (M, N, K, pre) in ((512, 512, 512, False), (300, 1024, 1024, True), (64, 1024, 512, False), (1, 512, 256, True)):
     qa, sa = O.quant_mx(O.normal_rows(1234, 0, M, K)); qb, sb = O.quant_mx(O.normal_rows(5678, 0, N, K))
     ref = O.gemm_mx(qa, qb, sa, sb, M, N, K, acc_f64=True)
     b = O.shuffle_weight_16x16(qb, N, K).reshape(N, K) if pre else qb
@@ -361,12 +361,12 @@ print("single-cta ok")
 
 
 def test_single_cta_path_when_pairs_disabled(dev):
-    """B2G_DISABLE_PAIR=1 routes M > 128 shapes to the single-CTA 128x256 kernel."""
+    """B2G_DISABLE_PAIR=1 / B2G_DISABLE_SKINNY=1 route every shape to the single-CTA kernel."""
     import os
     import subprocess
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    env = dict(os.environ, B2G_DISABLE_PAIR="1")
+    env = dict(os.environ, B2G_DISABLE_PAIR="1", B2G_DISABLE_SKINNY="1")
     r = subprocess.run([sys.executable, "-c", _SINGLE_CTA_SCRIPT, root], env=env, capture_output=True, text=True,
                        timeout=600)
     assert r.returncode == 0, r.stdout + r.stderr
@@ -393,6 +393,22 @@ def test_bounded_wait_pair_kernel(dev, oracle):
         L.b2g_set_wait_timeout_ms(4000)
     ref = oracle.gemm_mx(qa, qb, sa, sb, M, N, K, acc_f64=True)
     out = ops.mxfp8_gemm(*args, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    check_out(out, ref, torch.float32)
+
+
+@pytest.mark.parametrize("M", [1, 16, 64, 128])
+@pytest.mark.parametrize("bpre", [False, True])
+def test_skinny_decode_shapes(dev, oracle, M, bpre):
+    """Decode shapes (C4: N=28672, K=4096) on the transposed stream-K kernel, fp32 C."""
+    from gcnasm_b200 import ops
+    N, K = 28672, 4096
+    qa, sa, qb, sb = mx_operands(oracle, M, N, K)
+    ref = oracle.gemm_mx(qa, qb, sa, sb, M, N, K, acc_f64=True)
+    b = T(oracle.shuffle_weight_16x16(qb, N, K).reshape(N, K), dev) if bpre else T(qb, dev)
+    out = ops.mxfp8_gemm(T(qa, dev), b, T(oracle.sf_to_tc_layout(sa), dev), T(oracle.sf_to_tc_layout(sb), dev),
+                         out_dtype=torch.float32, b_preshuffled=bpre)
     torch.cuda.synchronize()
     assert ops.device_status() == 0
     check_out(out, ref, torch.float32)
