@@ -13,8 +13,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 LIB = os.path.join(HERE, "_lib", "libb2g.so")
 SOURCES = [os.path.join(HERE, "csrc", "b2g_api.cu")]
-DEPS = SOURCES + [os.path.join(HERE, "csrc", f) for f in ("b2g_gemm.cuh", "b2g_ptx.cuh", "b2g_aux.cuh")] + [
-    os.path.join(ROOT, "include", "b2g", "gemm.h")]
+# every source and header under csrc/ plus the public header: editing any of them rebuilds
+DEPS = sorted(os.path.join(HERE, "csrc", f) for f in os.listdir(os.path.join(HERE, "csrc"))
+              if f.endswith((".cu", ".cuh", ".h"))) + [os.path.join(ROOT, "include", "b2g", "gemm.h")]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

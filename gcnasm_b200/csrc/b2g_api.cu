@@ -26,6 +26,12 @@
 
 using namespace b2g;
 
+// Arrival counters of the skinny (decode) kernel's split tiles: one per
+// 128-row weight tile, zero at load, left at zero by every launch that
+// completes.  Shared by all calls on a device (they are stream-ordered).
+static constexpr int kSkinnyMaxTiles = 8192;  // N <= 1M
+static __device__ unsigned long long g_skinny_tile_cnt[kSkinnyMaxTiles];
+
 namespace {
 
 constexpr int kVersion = 100;  // 0.1.0
@@ -84,6 +90,7 @@ struct DevState {
   int* status = nullptr;  // device status word written by bounded waits
   void* ws = nullptr;     // scratch: split-K workspace and per-call scale re-layout
   size_t ws_bytes = 0;
+  unsigned long long* tile_cnt = nullptr;  // device address of g_skinny_tile_cnt
   FnCache fns;
 };
 
@@ -95,9 +102,20 @@ struct Env {
   int sms = 0;
   int* status = nullptr;
   FnCache* fns = nullptr;
+  unsigned long long* tile_cnt = nullptr;
   uint8_t* fixed_ws = nullptr;  // non-null: scratch of fixed capacity, never allocated
   size_t fixed_ws_bytes = 0;
 };
+
+// device address of the skinny kernel's tile counters on the current device
+int skinny_counters(unsigned long long** out) {
+  void* ptr = nullptr;
+  const cudaError_t err = cudaGetSymbolAddress(&ptr, g_skinny_tile_cnt);
+  if (err != cudaSuccess || !ptr)
+    return fail(B2G_ERR_CUDA, "cudaGetSymbolAddress(tile counters) failed: %s", cudaGetErrorString(err));
+  *out = static_cast<unsigned long long*>(ptr);
+  return B2G_OK;
+}
 
 std::mutex g_mu;
 DevState g_dev[64];
@@ -115,6 +133,8 @@ int device_state(DevState** out, int* dev_out = nullptr) {
     B2G_CUDA(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev));
     B2G_CUDA(cudaMalloc(&d.status, sizeof(int)));
     B2G_CUDA(cudaMemset(d.status, 0, sizeof(int)));
+    int rc = skinny_counters(&d.tile_cnt);
+    if (rc) return rc;
     d.init = true;
   }
   *out = &d;
@@ -159,6 +179,7 @@ Env env_of(DevState* d) {
   e.sms = d->sms;
   e.status = d->status;
   e.fns = &d->fns;
+  e.tile_cnt = d->tile_cnt;
   return e;
 }
 
@@ -409,12 +430,34 @@ bool use_skinny(const Req& r) {
     const char* v = getenv("B2G_DISABLE_SKINNY");
     return v && v[0] == '1';
   }();
-  return !off && r.M <= 128 && r.batch == 1 && r.mode != kModeBlk;
+  return !off && r.M <= 128 && r.batch == 1 && r.mode != kModeBlk && cdiv(r.N, 128) <= kSkinnyMaxTiles;
+}
+
+// B2G_DISABLE_PDL=1 launches without programmatic stream serialization.
+bool use_pdl() {
+  static const bool off = [] {
+    const char* v = getenv("B2G_DISABLE_PDL");
+    return v && v[0] == '1';
+  }();
+  return !off;
+}
+
+int skinny_mp(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128; }
+
+// 128-K blocks per ring stage: two (one 32 KB request of B) when K splits into
+// whole pairs of blocks and the stage still leaves room for a deep ring.
+int skinny_kkb(const Req& r) { return (r.K % 256 == 0 && skinny_mp(r.M) <= 64) ? 2 : 1; }
+
+long long skinny_units(const Req& r) {
+  return static_cast<long long>(cdiv(r.N, 128)) * (cdiv(r.K, 128) / skinny_kkb(r));
 }
 
 // Scratch bytes run_gemm will ask for beyond r.ws_offset.
-size_t split_ws_bytes(const Req& r, int S) {
-  if (use_skinny(r)) return r.out_f32 ? 0 : static_cast<size_t>(r.M) * r.N * 4;  // fp32 sums before the cast
+size_t split_ws_bytes(const Req& r, int S, int sms) {
+  if (use_skinny(r)) {  // fp32 partial slots, two per CTA
+    const long long grid = std::min<long long>(skinny_units(r), sms);
+    return static_cast<size_t>(2 * grid) * skinny_mp(r.M) * 128 * 4;
+  }
   return (S > 1 && !r.out_f32) ? static_cast<size_t>(S) * r.batch * r.M * r.N * 4 : 0;
 }
 
@@ -424,88 +467,117 @@ int launch_skinny(const Env& d, const CUtensorMap& tw, const CUtensorMap& ta, co
   const void* fn = reinterpret_cast<const void*>(&b2g_gemm_skinny_kernel<Cfg>);
   int rc = ensure_smem_attr(d.fns, fn, Cfg::kSmemBytes);
   if (rc) return rc;
-  b2g_gemm_skinny_kernel<Cfg><<<grid, Cfg::kThreads, Cfg::kSmemBytes, st>>>(tw, ta, sp);
-  B2G_CUDA(cudaGetLastError());
+  // programmatic dependent launch: this kernel's prologue overlaps the tail of
+  // the previous kernel on the stream (the kernel waits before touching memory)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(Cfg::kThreads);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = use_pdl() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  B2G_CUDA(cudaLaunchKernelEx(&cfg, b2g_gemm_skinny_kernel<Cfg>, tw, ta, sp));
   return B2G_OK;
 }
 
 template <int kMode, bool kPre>
-int dispatch_skinny_mp(const Env& d, int mp, const CUtensorMap& tw, const CUtensorMap& ta, const SkinnyParams& sp,
-                       int grid, cudaStream_t st) {
+int dispatch_skinny_mp(const Env& d, int mp, int kkb, const CUtensorMap& tw, const CUtensorMap& ta,
+                       const SkinnyParams& sp, int grid, cudaStream_t st) {
+  if (kkb == 2) {
+    switch (mp) {
+      case 16: return launch_skinny<SkinnyCfg<kMode, 16, kPre, 2>>(d, tw, ta, sp, grid, st);
+      case 32: return launch_skinny<SkinnyCfg<kMode, 32, kPre, 2>>(d, tw, ta, sp, grid, st);
+      default: return launch_skinny<SkinnyCfg<kMode, 64, kPre, 2>>(d, tw, ta, sp, grid, st);
+    }
+  }
   switch (mp) {
-    case 16: return launch_skinny<SkinnyCfg<kMode, 16, kPre>>(d, tw, ta, sp, grid, st);
-    case 32: return launch_skinny<SkinnyCfg<kMode, 32, kPre>>(d, tw, ta, sp, grid, st);
-    case 64: return launch_skinny<SkinnyCfg<kMode, 64, kPre>>(d, tw, ta, sp, grid, st);
-    default: return launch_skinny<SkinnyCfg<kMode, 128, kPre>>(d, tw, ta, sp, grid, st);
+    case 16: return launch_skinny<SkinnyCfg<kMode, 16, kPre, 1>>(d, tw, ta, sp, grid, st);
+    case 32: return launch_skinny<SkinnyCfg<kMode, 32, kPre, 1>>(d, tw, ta, sp, grid, st);
+    case 64: return launch_skinny<SkinnyCfg<kMode, 64, kPre, 1>>(d, tw, ta, sp, grid, st);
+    default: return launch_skinny<SkinnyCfg<kMode, 128, kPre, 1>>(d, tw, ta, sp, grid, st);
   }
 }
 
+std::atomic<unsigned long long> g_skinny_tag{0};
+
 int run_skinny(const Req& r, const Env& d) {
   int rc = B2G_OK;
-  const int mp = r.M <= 16 ? 16 : r.M <= 32 ? 32 : r.M <= 64 ? 64 : 128;
+  const int mp = skinny_mp(r.M);
+  const int kkb = skinny_kkb(r);
   SkinnyParams sp;
   memset(&sp, 0, sizeof(sp));
   sp.M = r.M; sp.N = r.N; sp.K = r.K;
+  sp.out = r.c;
+  sp.ldo = r.ldc;
+  sp.out_f32 = r.out_f32 ? 1 : 0;
   sp.alpha = r.alpha;
   sp.sfw = r.sfb;
   sp.sfa = r.sfa;
   sp.sf_rb = static_cast<long long>(cdiv(r.K, 128)) * 512;
   sp.NT = cdiv(r.N, 128);
-  sp.KB = cdiv(r.K, 128);
-  sp.units = static_cast<long long>(sp.NT) * sp.KB;
+  sp.KG = cdiv(r.K, 128) / kkb;
+  sp.kview = r.K % 128 == 0 ? 1 : 0;
+  sp.units = static_cast<long long>(sp.NT) * sp.KG;
+  sp.cnt = d.tile_cnt;
+  // tags are nonzero and below 2^48 (the counter keeps 16 bits of arrivals)
+  sp.tag = (g_skinny_tag.fetch_add(1) % ((1ull << 48) - 1)) + 1;
   sp.status = d.status;
   sp.timeout_ns = g_timeout_ns.load();
   sp.debug_stall = g_force_stall.load();
 
+  // Operand maps.  With K % 128 == 0 they view a row-major [rows][K] operand as
+  // (128 bytes, rows, K/128 blocks) so one box brings kkb whole K blocks, each
+  // landing as its own [rows][128 B] swizzled tile; otherwise (kkb == 1) plain
+  // (K, rows) maps whose out-of-range tail reads as zero.
   CUtensorMap tw, ta;
+  const long long kb_total = cdiv(r.K, 128);
   if (!r.bpre) {
-    cuuint64_t dims[3] = {(cuuint64_t)r.K, (cuuint64_t)r.N, 1};
-    cuuint64_t str[2] = {(cuuint64_t)r.ldb, (cuuint64_t)(r.ldb * r.N)};
-    cuuint32_t box[3] = {128, 128, 1};
-    rc = encode(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, r.b, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (sp.kview) {
+      cuuint64_t dims[3] = {128, (cuuint64_t)r.N, (cuuint64_t)kb_total};
+      cuuint64_t str[2] = {(cuuint64_t)r.ldb, 128};
+      cuuint32_t box[3] = {128, 128, (cuuint32_t)kkb};
+      rc = encode(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, r.b, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    } else {
+      cuuint64_t dims[3] = {(cuuint64_t)r.K, (cuuint64_t)r.N, 1};
+      cuuint64_t str[2] = {(cuuint64_t)r.ldb, (cuuint64_t)(r.ldb * r.N)};
+      cuuint32_t box[3] = {128, 128, 1};
+      rc = encode(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, r.b, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    }
   } else {
     cuuint64_t dims[4] = {256, (cuuint64_t)(r.N / 16), (cuuint64_t)(r.K / 16), 1};
     cuuint64_t str[3] = {(cuuint64_t)16 * r.K, 256, (cuuint64_t)((long long)r.N * r.K)};
-    cuuint32_t box[4] = {256, 8, 8, 1};
+    cuuint32_t box[4] = {256, 8, (cuuint32_t)(8 * kkb), 1};
     rc = encode(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, r.b, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
   }
   if (rc) return rc;
-  {
+  if (sp.kview) {
+    cuuint64_t dims[3] = {128, (cuuint64_t)r.M, (cuuint64_t)kb_total};
+    cuuint64_t str[2] = {(cuuint64_t)r.lda, 128};
+    cuuint32_t box[3] = {128, (cuuint32_t)mp, (cuuint32_t)kkb};
+    rc = encode(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, r.a, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  } else {
     cuuint64_t dims[3] = {(cuuint64_t)r.K, (cuuint64_t)r.M, 1};
     cuuint64_t str[2] = {(cuuint64_t)r.lda, (cuuint64_t)(r.lda * r.M)};
     cuuint32_t box[3] = {128, (cuuint32_t)mp, 1};
     rc = encode(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, r.a, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (rc) return rc;
   }
-  // partial sums are added into zeroed fp32: C itself, or scratch cast to bf16 afterwards
-  float* acc = nullptr;
-  long long ldacc = 0;
-  if (r.out_f32) {
-    acc = static_cast<float*>(r.c);
-    ldacc = r.ldc;
-  } else {
-    void* ws = nullptr;
-    rc = env_workspace(d, r.ws_offset + static_cast<size_t>(r.M) * r.N * 4, &ws);
-    if (rc) return rc;
-    acc = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + r.ws_offset);
-    ldacc = r.N;
-  }
-  B2G_CUDA(cudaMemset2DAsync(acc, ldacc * 4, 0, static_cast<size_t>(r.N) * 4, r.M, r.stream));
-  sp.c = acc;
-  sp.ldc = ldacc;
-  const int grid = static_cast<int>(std::min<long long>(sp.units, d.sms));
-  if (r.mode == kModeMX)
-    rc = r.bpre ? dispatch_skinny_mp<kModeMX, true>(d, mp, tw, ta, sp, grid, r.stream)
-                : dispatch_skinny_mp<kModeMX, false>(d, mp, tw, ta, sp, grid, r.stream);
-  else
-    rc = r.bpre ? dispatch_skinny_mp<kModePlain, true>(d, mp, tw, ta, sp, grid, r.stream)
-                : dispatch_skinny_mp<kModePlain, false>(d, mp, tw, ta, sp, grid, r.stream);
   if (rc) return rc;
-  if (!r.out_f32) {
-    const long long work = static_cast<long long>(r.M) * (r.N / 4);
-    b2g_splitk_reduce_kernel<false><<<grid_for(work, 256, d.sms), 256, 0, r.stream>>>(acc, r.c, 1, 1, r.M, r.N, r.ldc, 0);
-    B2G_CUDA(cudaGetLastError());
-  }
+
+  const int grid = static_cast<int>(std::min<long long>(sp.units, d.sms));
+  void* ws = nullptr;
+  rc = env_workspace(d, r.ws_offset + split_ws_bytes(r, 1, d.sms), &ws);
+  if (rc) return rc;
+  sp.part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + r.ws_offset);
+  if (r.mode == kModeMX)
+    rc = r.bpre ? dispatch_skinny_mp<kModeMX, true>(d, mp, kkb, tw, ta, sp, grid, r.stream)
+                : dispatch_skinny_mp<kModeMX, false>(d, mp, kkb, tw, ta, sp, grid, r.stream);
+  else
+    rc = r.bpre ? dispatch_skinny_mp<kModePlain, true>(d, mp, kkb, tw, ta, sp, grid, r.stream)
+                : dispatch_skinny_mp<kModePlain, false>(d, mp, kkb, tw, ta, sp, grid, r.stream);
+  if (rc) return rc;
   return maybe_sync_check();
 }
 
@@ -620,7 +692,7 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
                                  static_cast<size_t>(r.N) * 4, r.M, r.stream));
   } else if (p.out_mode == kOutWorkspace) {
     void* ws = nullptr;
-    const size_t need = r.ws_offset + split_ws_bytes(r, S);
+    const size_t need = r.ws_offset + split_ws_bytes(r, S, d.sms);
     rc = env_workspace(d, need, &ws);
     if (rc) return rc;
     p.ws = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + r.ws_offset);
@@ -688,6 +760,7 @@ struct NoAllocDev {
   bool ready = false;
   int sms = 0;
   uint8_t* base = nullptr;  // device address of g_noalloc_scratch on this device
+  unsigned long long* tile_cnt = nullptr;
   FnCache fns;
 };
 NoAllocDev g_noalloc[64];
@@ -710,12 +783,15 @@ int noalloc_env(Env* e) {
     if (err != cudaSuccess || !ptr)
       return fail(B2G_ERR_CUDA, "cudaGetSymbolAddress(no-alloc scratch) failed: %s", cudaGetErrorString(err));
     d.base = static_cast<uint8_t*>(ptr);
+    int rc = skinny_counters(&d.tile_cnt);
+    if (rc) return rc;
     d.ready = true;
   }
   e->dev = nullptr;
   e->sms = d.sms;
   e->status = reinterpret_cast<int*>(d.base);
   e->fns = &d.fns;
+  e->tile_cnt = d.tile_cnt;
   e->fixed_ws = d.base + kNoAllocStatusBytes;
   e->fixed_ws_bytes = kNoAllocScratchBytes - kNoAllocStatusBytes;
   return B2G_OK;
@@ -761,7 +837,11 @@ int b2g_device_status(int* status, int clear) {
   if (rc) return rc;
   B2G_CUDA(cudaDeviceSynchronize());
   B2G_CUDA(cudaMemcpy(status, d->status, sizeof(int), cudaMemcpyDeviceToHost));
-  if (clear) B2G_CUDA(cudaMemset(d->status, 0, sizeof(int)));
+  if (clear) {
+    B2G_CUDA(cudaMemset(d->status, 0, sizeof(int)));
+    // a launch that stopped early can leave tile counters mid-count
+    if (*status) B2G_CUDA(cudaMemset(d->tile_cnt, 0, sizeof(unsigned long long) * kSkinnyMaxTiles));
+  }
   return *status ? B2G_ERR_DEVICE_TIMEOUT : B2G_OK;
 }
 
@@ -901,7 +981,7 @@ int b2g_gemm_mxfp8_f4gemm(const b2g_f4gemm_kargs* a, int bpreshuffle, int out_dt
   const size_t offB = static_cast<size_t>((tcA + 255) / 256 * 256);
   const size_t offW = offB + static_cast<size_t>((tcB + 255) / 256 * 256);
   void* ws = nullptr;
-  rc = workspace(d, offW + split_ws_bytes(r, S), &ws);
+  rc = workspace(d, offW + split_ws_bytes(r, S, d->sms), &ws);
   if (rc) return rc;
   uint8_t* sA = static_cast<uint8_t*>(ws);
   uint8_t* sB = sA + offB;
@@ -939,7 +1019,7 @@ int b2g_gemm_mxfp8_noalloc(const b2g_mxfp8_args* g, void* stream) {
   int bn = 0, S = 1, kb_per = 1;
   rc = plan_tiles(r, e.sms, &bn, &S, &kb_per);
   if (rc) return rc;
-  const size_t need = split_ws_bytes(r, S);
+  const size_t need = split_ws_bytes(r, S, e.sms);
   if (need > e.fixed_ws_bytes)
     return fail(B2G_ERR_WORKSPACE,
                 "b2g_gemm_mxfp8_noalloc: %d-way split-K partials need %zu bytes; its fixed scratch holds %zu "

@@ -4,14 +4,20 @@
 //
 // The product is computed transposed: the MMA's M = 128 runs over 128 rows of
 // B (weights) and its N = MP (M rounded up to 16/32/64/128) over the rows of A,
-// so no tensor-core rows are spent on padding.  The work -- (128-row B tile,
-// 128-K block) units -- is split evenly over the persistent CTAs (stream-K):
-// CTA c takes units [c*W/G, (c+1)*W/G), which may begin or end inside a B tile.
-// Every contiguous run of units of one tile ("segment") accumulates in TMEM and
-// is added to C (zeroed by the caller) with fp32 vector reductions; with at
-// most two segments per tile the sum is order-independent.  Decode GEMMs are
-// bound by streaming B from HBM, so the ring is deep (8 stages of 16 KB of B)
-// and every SM streams an equal share of B.
+// so no tensor-core rows are spent on padding.  Work units are (128-row B tile,
+// group of kKB 128-K blocks); they are split evenly over the persistent CTAs
+// (stream-K): CTA c takes units [c*U/G, (c+1)*U/G), which may begin or end
+// inside a tile.  Each contiguous run of one tile's units ("segment")
+// accumulates in TMEM.  A tile covered by a single segment is written straight
+// to C.  Otherwise every segment stores its fp32 partial to scratch and counts
+// itself in the tile's arrival counter; the last to arrive adds the partials
+// in segment order (a fixed order, so results do not depend on timing),
+// applies alpha and writes C in the output type.  One launch per call: no
+// zeroing pass, no atomics on C, no separate cast.
+//
+// Decode GEMMs are bound by streaming B from HBM: every SM streams an equal
+// share of B through a deep ring (128-256 KB of B in flight per SM), and a
+// stage carries up to two K blocks so one TMA request moves 32 KB of B.
 // Modes: kModePlain (alpha only) and kModeMX (UE8M0 1x32 scales; the weights'
 // scale atoms are the MMA's A scales, the activations' its B scales).
 #pragma once
@@ -20,17 +26,21 @@
 
 namespace b2g {
 
-template <int kMode_, int kMP_, bool kBPre_>
+template <int kMode_, int kMP_, bool kBPre_, int kKB_>
 struct SkinnyCfg {
   static constexpr int kMode = kMode_;
   static constexpr int kMP = kMP_;  // padded A rows = MMA N
   static constexpr bool kBPre = kBPre_;
+  static constexpr int kKB = kKB_;  // 128-K blocks per stage
   static constexpr int kThreads = 192;  // producer, MMA, 4 epilogue warps
-  static constexpr int kWBytes = 128 * 128;         // one 128 x 128 B (weight) tile
-  static constexpr int kABytes = kMP * 128;         // the A rows of one 128-K block
-  static constexpr int kSfBytes = kMode == kModeMX ? 512 : 0;  // one atom each
+  static constexpr int kWBlk = 128 * 128;  // one 128 x 128 B (weight) tile
+  static constexpr int kABlk = kMP * 128;  // the A rows of one 128-K block
+  static constexpr int kWBytes = kKB * kWBlk;
+  static constexpr int kABytes = kKB * kABlk;
+  static constexpr int kSfBytes = kMode == kModeMX ? 512 * kKB : 0;  // kKB atoms each
   static constexpr int kStageBytes = kWBytes + kABytes + 2 * kSfBytes;
-  static constexpr int kStages = kMP <= 32 ? 10 : (kMP == 64 ? 8 : 6);
+  static constexpr int kMaxStages = kKB == 1 ? 8 : 5;
+  static constexpr int kStages = 225000 / kStageBytes < kMaxStages ? 225000 / kStageBytes : kMaxStages;
   static constexpr int kAccStages = 2;
   static constexpr int kAccStride = kMP < 32 ? 32 : kMP;  // accumulator stages start 32-column aligned
   static constexpr int kSfCols = kMode == kModeMX ? 8 : 0;  // weight atom (4) + activation atom (4)
@@ -47,30 +57,81 @@ struct SkinnyCfg {
   static constexpr int kNumBars = 2 * kStages + 2 * kAccStages + 2;
   static constexpr int kOffCtl = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffCtl + 16 + 1024;
+  static_assert(kStages >= 3, "ring depth");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
   static_assert(kMP == 16 || kMP == 32 || kMP == 64 || kMP == 128, "padded M");
-  static_assert(kABytes % 1024 == 0 || kMP == 16, "A stage alignment");
+  static_assert(kKB == 1 || kKB == 2, "K blocks per stage");
+  static_assert(kABlk % 1024 == 0 || kMP == 16, "A stage alignment");
 };
 
 struct SkinnyParams {
   int M, N, K;
-  float* c;          // fp32 [M][ldc], zeroed by the caller; partial sums are added
-  long long ldc;
+  void* out;           // C [M][ldo]: fp32 or bf16 (out_f32)
+  long long ldo;
+  int out_f32;
   float alpha;
   const uint8_t* sfw;  // weight (B) scales, tensor-core atom layout, atoms [n_block][k_block]
   const uint8_t* sfa;  // activation (A) scales, same layout (one row block)
   long long sf_rb;     // bytes between row blocks of either scale buffer
-  int NT, KB;          // 128-row weight tiles, 128-K blocks
-  long long units;     // NT * KB
+  int NT, KG;          // 128-row weight tiles; K groups (kKB blocks each) per tile
+  int kview;           // 1: operand maps are (128, rows, K/128) views, coordinates (0, row, k_block);
+                       // 0: (K, rows, 1) maps, coordinates (k_block * 128, row, 0)
+  long long units;     // NT * KG
+  float* part;         // partial slots [2 * gridDim.x][kMP][128] fp32
+  unsigned long long* cnt;  // per-tile arrival counters, (tag << 16) | arrivals
+  unsigned long long tag;   // this launch's counter tag (nonzero, < 2^48)
   int* status;
   unsigned long long timeout_ns;
   int debug_stall;
 };
 
-// contiguous unit range of CTA `c` out of `g`
-__device__ __forceinline__ void skinny_range(long long units, int c, int g, long long* lo, long long* hi) {
-  *lo = units * c / g;
-  *hi = units * (c + 1) / g;
+// CTA owning unit u when U units are split evenly over G CTAs (the largest c
+// with U*c/G <= u).
+__device__ __forceinline__ int skinny_owner(long long u, long long U, int G) {
+  return static_cast<int>(((u + 1) * G - 1) / U);
+}
+
+// Partial slot of CTA c's segment on tile nt: 2c for the CTA's first segment
+// (its range starts inside or at the start of tile nt), 2c + 1 for its last.
+__device__ __forceinline__ int skinny_slot(int c, int nt, long long U, int G, int KG) {
+  const long long lo = U * c / G;
+  return 2 * c + (lo / KG == nt ? 0 : 1);
+}
+
+// The four epilogue warps (128 threads) synchronise on named barrier 1.
+__device__ __forceinline__ void skinny_epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// True on every epilogue thread iff `ok` holds on all of them, so the warps
+// leave their loop together and never strand one another at a barrier.
+__device__ __forceinline__ bool skinny_epi_all(bool ok) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, 128, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(ok))
+      : "memory");
+  return r != 0;
+}
+
+// Count one arrival at a tile counter and return the arrivals so far this
+// launch.  A counter carrying another tag is stale (an earlier launch that
+// stopped early) and counts as zero.  `expect` is the caller's guess of the
+// arrivals before it, so the usual case costs one compare-and-swap round trip.
+// -1 if the CAS loop does not settle.
+__device__ __forceinline__ int skinny_arrive(unsigned long long* cnt, unsigned long long tag, int expect,
+                                             int* status) {
+  unsigned long long cur = expect > 0 ? (tag << 16) | static_cast<unsigned long long>(expect) : 0ull;
+  for (int it = 0; it < (1 << 20); ++it) {
+    const unsigned long long nxt = (cur >> 16) == tag ? cur + 1 : (tag << 16) | 1ull;
+    const unsigned long long prev = atomicCAS(cnt, cur, nxt);
+    if (prev == cur) return static_cast<int>(nxt & 0xFFFFull);
+    cur = prev;
+  }
+  atomicCAS(status, 0, static_cast<int>(kDevTimeoutEpilogue));
+  return -1;
 }
 
 template <class Cfg>
@@ -81,6 +142,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
   constexpr int ST = Cfg::kStages;
   constexpr int AS = Cfg::kAccStages;
   constexpr int MP = Cfg::kMP;
+  constexpr int KBS = Cfg::kKB;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
@@ -92,14 +154,44 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
   uint64_t* never = fin + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + Cfg::kOffCtl);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kOffCtl + 4);
+  volatile uint32_t* last_flag = reinterpret_cast<volatile uint32_t*>(smem + Cfg::kOffCtl + 8);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  if (kMode == kModeMX) {
-    for (int i = threadIdx.x; i < ST * 2 * Cfg::kSfBytes / 4; i += Cfg::kThreads)
-      reinterpret_cast<uint32_t*>(smem + Cfg::kOffSfw)[i] = 0x7F7F7F7Fu;
-    fence_proxy_async_smem();
-  }
+  const long long U = p.units;
+  const int G = gridDim.x;
+  const long long u_lo = U * blockIdx.x / G, u_hi = U * (blockIdx.x + 1) / G;
+  const uint64_t tmo = p.timeout_ns;
+
+  // One stage of loads: B tile(s), A rows and, for MX, both scale atoms (which
+  // fill the stage's scale buffers completely).  B is read once: evict first,
+  // so it does not push A, the scales and the partial slots out of L2.
+  const uint64_t pol_w = l2_policy_evict_first();
+  auto issue = [&](long long u, int s) {
+    const int nt = static_cast<int>(u / p.KG);
+    const int kb = static_cast<int>(u - static_cast<long long>(nt) * p.KG) * KBS;
+    mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
+    uint8_t* w_dst = smem + Cfg::kOffW + s * Cfg::kWBytes;
+    uint8_t* a_dst = smem + Cfg::kOffA + s * Cfg::kABytes;
+    if (Cfg::kBPre)
+      tma_load_4d_hint(w_dst, &tm_w, &full[s], 0, nt * 8, kb * 8, 0, pol_w);
+    else if (p.kview)
+      tma_load_3d_hint(w_dst, &tm_w, &full[s], 0, nt * 128, kb, pol_w);
+    else
+      tma_load_3d_hint(w_dst, &tm_w, &full[s], kb * 128, nt * 128, 0, pol_w);
+    if (p.kview)
+      tma_load_3d(a_dst, &tm_a, &full[s], 0, 0, kb);
+    else
+      tma_load_3d(a_dst, &tm_a, &full[s], kb * 128, 0, 0);
+    if (kMode == kModeMX) {
+      bulk_load(smem + Cfg::kOffSfw + s * Cfg::kSfBytes, p.sfw + nt * p.sf_rb + kb * 512, Cfg::kSfBytes, &full[s]);
+      bulk_load(smem + Cfg::kOffSfa + s * Cfg::kSfBytes, p.sfa + kb * 512, Cfg::kSfBytes, &full[s]);
+    }
+  };
+
+  // The producer thread initialises the barriers and fills the whole ring
+  // before the block-wide sync, so HBM traffic starts while TMEM is allocated.
+  const int pre = static_cast<int>(u_hi - u_lo < ST ? u_hi - u_lo : ST);
   if (threadIdx.x == 0) {
     for (int s = 0; s < ST; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
     for (int s = 0; s < AS; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], 4); }
@@ -107,36 +199,28 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     mbar_init(never, 1);
     *abort_flag = 0;
     fence_mbar_init();
+    tma_prefetch_desc(&tm_w);
+    tma_prefetch_desc(&tm_a);
+    griddep_wait();  // launched as a programmatic dependent: the previous kernel's writes are visible after this
+    for (int i = 0; i < pre; ++i) issue(u_lo + i, i);
   }
   if (warp == 1) tmem_alloc<Cfg::kTmemCols>(tmem_holder);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
-  const uint64_t tmo = p.timeout_ns;
-  long long u_lo, u_hi;
-  skinny_range(p.units, blockIdx.x, gridDim.x, &u_lo, &u_hi);
+  griddep_wait();
+  griddep_launch_dependents();  // the next kernel may start its prologue as SMs free up
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      tma_prefetch_desc(&tm_w);
-      tma_prefetch_desc(&tm_a);
-      int s = 0;
-      uint32_t ph = 0, issued_mask = 0, issued_phase = 0;
-      for (long long u = u_lo; u < u_hi; ++u) {
-        const int nt = static_cast<int>(u / p.KB), kb = static_cast<int>(u - static_cast<long long>(nt) * p.KB);
+      int s = pre % ST;
+      uint32_t ph = pre == ST ? 1u : 0u;
+      uint32_t issued_mask = pre == ST ? (1u << ST) - 1u : (1u << pre) - 1u, issued_phase = 0;
+      for (long long u = u_lo + pre; u < u_hi; ++u) {
         if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, kDevTimeoutProducer, tmo)) break;
-        mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
-        if (Cfg::kBPre)
-          tma_load_4d(smem + Cfg::kOffW + s * Cfg::kWBytes, &tm_w, &full[s], 0, nt * 8, kb * 8, 0);
-        else
-          tma_load_3d(smem + Cfg::kOffW + s * Cfg::kWBytes, &tm_w, &full[s], kb * 128, nt * 128, 0);
-        tma_load_3d(smem + Cfg::kOffA + s * Cfg::kABytes, &tm_a, &full[s], kb * 128, 0, 0);
-        if (kMode == kModeMX) {
-          bulk_load(smem + Cfg::kOffSfw + s * Cfg::kSfBytes, p.sfw + nt * p.sf_rb + kb * 512, 512, &full[s]);
-          bulk_load(smem + Cfg::kOffSfa + s * Cfg::kSfBytes, p.sfa + kb * 512, 512, &full[s]);
-        }
+        issue(u, s);
         issued_mask |= 1u << s;
         issued_phase = (issued_phase & ~(1u << s)) | (ph << s);
         if (++s == ST) { s = 0; ph ^= 1; }
@@ -159,35 +243,39 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       if (p.debug_stall) ok = mbar_wait(never, 0, abort_flag, p.status, kDevTimeoutMma, tmo);
       long long u = u_lo;
       while (ok && u < u_hi) {
-        const int nt = static_cast<int>(u / p.KB);
-        const long long seg_end = u_hi < static_cast<long long>(nt + 1) * p.KB ? u_hi : static_cast<long long>(nt + 1) * p.KB;
+        const int nt = static_cast<int>(u / p.KG);
+        const long long tile_end = static_cast<long long>(nt + 1) * p.KG;
+        const long long seg_end = u_hi < tile_end ? u_hi : tile_end;
         if (!mbar_wait(&acc_empty[as], aph ^ 1, abort_flag, p.status, kDevTimeoutMma, tmo)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + as * Cfg::kAccStride;
         for (long long v = u; v < seg_end; ++v) {
           if (!mbar_wait(&full[s], ph, abort_flag, p.status, kDevTimeoutMma, tmo)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t w_base = smem_u32(smem + Cfg::kOffW + s * Cfg::kWBytes);
-          const uint32_t a_base = smem_u32(smem + Cfg::kOffA + s * Cfg::kABytes);
-          const uint32_t sf_off = sfbuf * Cfg::kSfCols;
-          sfbuf ^= 1;
-          if (kMode == kModeMX) {
-            tc_cp_32x128b_warpx4(tmem_base + Cfg::kSfCol + sf_off,
-                                 desc_sf_atom(smem_u32(smem + Cfg::kOffSfw + s * Cfg::kSfBytes)));
-            tc_cp_32x128b_warpx4(tmem_base + Cfg::kSfCol + sf_off + 4,
-                                 desc_sf_atom(smem_u32(smem + Cfg::kOffSfa + s * Cfg::kSfBytes)));
-          }
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t wdesc = Cfg::kBPre ? desc_kmajor_interleave(w_base + kk * 2 * (128 * 16), 128 * 16)
-                                              : desc_kmajor_sw128(w_base + kk * 32);
-            const uint64_t adesc = desc_kmajor_sw128(a_base + kk * 32);
-            const uint32_t acc = (v > u || kk > 0);
-            if (kMode == kModeMX)
-              mma_mxf8f6f4(d_tmem, wdesc, adesc, idesc_mxf8f6f4(128, MP, kk, kk), tmem_base + Cfg::kSfCol + sf_off,
-                           tmem_base + Cfg::kSfCol + sf_off + 4, acc);
-            else
-              mma_f8f6f4(d_tmem, wdesc, adesc, idesc_f8f6f4(128, MP), acc);
+          for (int j = 0; j < KBS; ++j) {
+            const uint32_t w_base = smem_u32(smem + Cfg::kOffW + s * Cfg::kWBytes + j * Cfg::kWBlk);
+            const uint32_t a_base = smem_u32(smem + Cfg::kOffA + s * Cfg::kABytes + j * Cfg::kABlk);
+            const uint32_t sf_off = sfbuf * Cfg::kSfCols;
+            sfbuf ^= 1;
+            if (kMode == kModeMX) {
+              tc_cp_32x128b_warpx4(tmem_base + Cfg::kSfCol + sf_off,
+                                   desc_sf_atom(smem_u32(smem + Cfg::kOffSfw + s * Cfg::kSfBytes + j * 512)));
+              tc_cp_32x128b_warpx4(tmem_base + Cfg::kSfCol + sf_off + 4,
+                                   desc_sf_atom(smem_u32(smem + Cfg::kOffSfa + s * Cfg::kSfBytes + j * 512)));
+            }
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t wdesc = Cfg::kBPre ? desc_kmajor_interleave(w_base + kk * 2 * (128 * 16), 128 * 16)
+                                                : desc_kmajor_sw128(w_base + kk * 32);
+              const uint64_t adesc = desc_kmajor_sw128(a_base + kk * 32);
+              const uint32_t acc = (v > u || j > 0 || kk > 0);
+              if (kMode == kModeMX)
+                mma_mxf8f6f4(d_tmem, wdesc, adesc, idesc_mxf8f6f4(128, MP, kk, kk), tmem_base + Cfg::kSfCol + sf_off,
+                             tmem_base + Cfg::kSfCol + sf_off + 4, acc);
+              else
+                mma_f8f6f4(d_tmem, wdesc, adesc, idesc_f8f6f4(128, MP), acc);
+            }
           }
           tc_commit(&empty[s]);
           if (++s == ST) { s = 0; ph ^= 1; }
@@ -204,37 +292,129 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue: 4 warps, one TMEM lane group each
+    // Columns are handled CH at a time so one CH-wide register array is live.
+    constexpr int CH = MP < 32 ? MP : 32;
     const int quad = warp & 3;
+    const int r = quad * 32 + lane;  // TMEM lane = weight row in the tile = output column in the tile
+    const int et = threadIdx.x - 64;
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
     int as = 0;
     uint32_t aph = 0;
     long long u = u_lo;
     while (u < u_hi) {
-      const int nt = static_cast<int>(u / p.KB);
-      const long long seg_end = u_hi < static_cast<long long>(nt + 1) * p.KB ? u_hi : static_cast<long long>(nt + 1) * p.KB;
-      if (!mbar_wait(&acc_full[as], aph, abort_flag, p.status, kDevTimeoutEpilogue, tmo)) break;
+      const int nt = static_cast<int>(u / p.KG);
+      const long long t0 = static_cast<long long>(nt) * p.KG;
+      const long long seg_end = u_hi < t0 + p.KG ? u_hi : t0 + p.KG;
+      const int c0 = skinny_owner(t0, U, G), c1 = skinny_owner(t0 + p.KG - 1, U, G);
+      const int nseg = c1 - c0 + 1;
+      // This CTA's last segment of a split tile finishes late, when the other
+      // segments' partials have long left L2: bring them back while its MMAs run.
+      if (nseg > 1 && seg_end == u_hi && et < nseg && c0 + et != static_cast<int>(blockIdx.x))
+        bulk_prefetch_l2(p.part + static_cast<long long>(skinny_slot(c0 + et, nt, U, G, p.KG)) * MP * 128,
+                         MP * 128 * 4);
+      const bool got = mbar_wait(&acc_full[as], aph, abort_flag, p.status, kDevTimeoutEpilogue, tmo);
+      if (!skinny_epi_all(got)) break;
       tc_fence_after();
-      uint32_t v[MP];
-      if (MP >= 32) {
+      const uint32_t acc_addr = tmem_base + lane_addr + as * Cfg::kAccStride;
+      const int n = nt * 128 + r;
+      const bool col_ok = n < p.N;
+
+      // output columns [mc, mc + CH) of this thread's output column n
+      auto store_out = [&](int mc, const float (&x)[CH]) {
+        if (!col_ok) return;
+        if (p.out_f32) {
+          float* col = static_cast<float*>(p.out) + n;
 #pragma unroll
-        for (int c = 0; c < MP / 32; ++c)
-          tmem_ld_32x32b_x32(tmem_base + lane_addr + as * Cfg::kAccStride + c * 32,
-                             *reinterpret_cast<uint32_t(*)[32]>(&v[c * 32]));
+          for (int i = 0; i < CH; ++i)
+            if (mc + i < p.M) col[(mc + i) * p.ldo] = x[i] * p.alpha;
+        } else {
+          __nv_bfloat16* col = static_cast<__nv_bfloat16*>(p.out) + n;
+#pragma unroll
+          for (int i = 0; i < CH; ++i)
+            if (mc + i < p.M) col[(mc + i) * p.ldo] = __float2bfloat16_rn(x[i] * p.alpha);
+        }
+      };
+      auto load_chunk = [&](int mc, uint32_t (&x)[CH]) {
+        if (CH == 32)
+          tmem_ld_32x32b_x32(acc_addr + mc, *reinterpret_cast<uint32_t(*)[32]>(&x[0]));
+        else
+          tmem_ld_32x32b_x16(acc_addr + mc, *reinterpret_cast<uint32_t(*)[16]>(&x[0]));
+        tc_wait_ld();
+      };
+
+      if (nseg == 1) {
+#pragma unroll 1
+        for (int mc = 0; mc < MP; mc += CH) {
+          uint32_t v[CH];
+          load_chunk(mc, v);
+          float x[CH];
+#pragma unroll
+          for (int i = 0; i < CH; ++i) x[i] = __uint_as_float(v[i]);
+          store_out(mc, x);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[as]);
       } else {
-        tmem_ld_32x32b_x16(tmem_base + lane_addr + as * Cfg::kAccStride, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
-      }
-      tc_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[as]);
-      if (++as == AS) { as = 0; aph ^= 1; }
-      const int n = nt * 128 + quad * 32 + lane;  // this thread's weight row = output column
-      if (n < p.N) {
-        float* col = p.c + n;
+        // Partial -> slot (first segment of this CTA: 2c, its last: 2c + 1); all
+        // MP rows, unpredicated, so the stores and the loads below pipeline.
+        const int slot = skinny_slot(static_cast<int>(blockIdx.x), nt, U, G, p.KG);
+        float* mine = p.part + static_cast<long long>(slot) * MP * 128 + r;
+#pragma unroll 1
+        for (int mc = 0; mc < MP; mc += CH) {
+          uint32_t v[CH];
+          load_chunk(mc, v);
 #pragma unroll
-        for (int m = 0; m < MP; ++m)
-          if (m < p.M) atomicAdd(col + m * p.ldc, __uint_as_float(v[m]) * p.alpha);
+          for (int i = 0; i < CH; ++i) __stcg(mine + (mc + i) * 128, __uint_as_float(v[i]));
+        }
+        // Count in: the barrier orders the four warps' stores before thread 0's
+        // release fence and arrival; its acquire fence and the second barrier
+        // order the reads of the other partials after the arrivals it saw.
+        skinny_epi_bar();
+        if (et == 0) {
+          fence_acq_rel_gpu();
+          // a CTA's last segment usually arrives after the tile's other pieces, its first before them
+          const int arrivals = skinny_arrive(p.cnt + nt, p.tag, seg_end == u_hi ? nseg - 1 : 0, p.status);
+          const bool last = arrivals == nseg;
+          if (last) fence_acq_rel_gpu();
+          *last_flag = last ? 1u : 0u;
+        }
+        skinny_epi_bar();
+        if (*last_flag != 0) {
+          // the partials added in segment order; this CTA's own comes from TMEM
+          // (the accumulator stage is released only after this)
+#pragma unroll 1
+          for (int mc = 0; mc < MP; mc += CH) {
+            float x[CH];
+#pragma unroll
+            for (int i = 0; i < CH; ++i) x[i] = 0.f;
+            for (int jj = 0; jj < nseg; ++jj) {
+              const int cj = c0 + jj;
+              if (cj == static_cast<int>(blockIdx.x)) {
+                uint32_t v[CH];
+                load_chunk(mc, v);
+#pragma unroll
+                for (int i = 0; i < CH; ++i) x[i] += __uint_as_float(v[i]);
+              } else {
+                const float* pj = p.part + static_cast<long long>(skinny_slot(cj, nt, U, G, p.KG)) * MP * 128 +
+                                  mc * 128 + r;
+                float y[CH];
+#pragma unroll
+                for (int i = 0; i < CH; ++i) y[i] = __ldcg(pj + i * 128);
+#pragma unroll
+                for (int i = 0; i < CH; ++i) x[i] += y[i];
+              }
+            }
+            store_out(mc, x);
+          }
+          // all arrivals are in: leave the counter at zero for the next launch (or a replay)
+          if (et == 0) *reinterpret_cast<volatile unsigned long long*>(p.cnt + nt) = 0ull;
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[as]);
       }
+      if (++as == AS) { as = 0; aph ^= 1; }
       u = seg_end;
     }
   }

@@ -99,20 +99,36 @@ class Clocks:
         return f"sm {sm:.0f} MHz  {pw:.0f} W"
 
 
-def time_rounds(fn, warmup, iters, rounds, flush_bytes=0):
-    """Best / median / worst per-call milliseconds over `rounds` rounds of `iters` calls."""
+def time_rounds(fn, warmup, iters, rounds, flush_bytes=0, graph=False):
+    """Best / median / worst per-call milliseconds over `rounds` rounds of `iters` calls.
+
+    graph=True captures the `iters` calls in one CUDA graph and times its
+    replay: device time per call without the host's per-call cost (a GEMM of a
+    few microseconds is otherwise bounded by the Python + ctypes call)."""
     buf = torch.empty(flush_bytes, dtype=torch.uint8, device="cuda") if flush_bytes else None
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
+    run = None
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(iters):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+        run = g.replay
     res = []
     for _ in range(rounds):
         if buf is not None:
             buf.fill_(1)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
-        for _ in range(iters):
-            fn()
+        if run is not None:
+            run()
+        else:
+            for _ in range(iters):
+                fn()
         b.record()
         torch.cuda.synchronize()
         res.append(a.elapsed_time(b) / iters)
@@ -144,6 +160,7 @@ def main(argv=None):
     ap.add_argument("--iters", type=int, default=int(env.get("BENCH_ITERS", 20)))
     ap.add_argument("--rounds", type=int, default=int(env.get("BENCH_ROUNDS", 5)))
     ap.add_argument("--flush-l2", action="store_true", help="write 256 MiB before each round")
+    ap.add_argument("--graph", action="store_true", help="replay the timed calls from a CUDA graph")
     ap.add_argument("--sweep", action="store_true", help="time split candidates 0..4 and report the best")
     ap.add_argument("--csv", default="", help="append sweep results to this CSV")
     a = ap.parse_args(argv)
@@ -162,13 +179,14 @@ def main(argv=None):
         fn = make_call(a.mode, ab, out, l2, a.group_n, bool(a.bpreshuffle))
         try:
             with Clocks() as clk:
-                best, med, worst = time_rounds(fn, a.warmup, a.iters, a.rounds, 256 << 20 if a.flush_l2 else 0)
+                best, med, worst = time_rounds(fn, a.warmup, a.iters, a.rounds, 256 << 20 if a.flush_l2 else 0,
+                                               a.graph)
         except capi.B2GError as e:
             print(f"split {l2}: {e}")
             continue
         tf = lambda t: flops / (t * 1e-3) / 1e12  # noqa: E731
         gb = lambda t: nbytes / (t * 1e-3) / 1e9  # noqa: E731
-        print(f"[{a.mode} M={M} N={N} K={K} out={a.out} log2_split={l2} bpre={a.bpreshuffle}] "
+        print(f"[{a.mode} M={M} N={N} K={K} out={a.out} log2_split={l2} bpre={a.bpreshuffle}{' graph' if a.graph else ''}] "
               f"best={best * 1e3:.2f} us  median={med * 1e3:.2f} us  worst={worst * 1e3:.2f} us  "
               f"{tf(best):.1f} TFLOP/s  {gb(best):.1f} GB/s  [{clk.summary()}]")
         rows.append([a.mode, M, N, K, a.out, a.bpreshuffle, l2, f"{best * 1e3:.3f}", f"{tf(best):.2f}",

@@ -412,3 +412,70 @@ def test_skinny_decode_shapes(dev, oracle, M, bpre):
     torch.cuda.synchronize()
     assert ops.device_status() == 0
     check_out(out, ref, torch.float32)
+
+
+# Split-tile fixup of the skinny kernel: a tile's K range shared by several CTAs
+# (up to 64 segments when N is small and K large), K not a multiple of 256 (one
+# K block per ring stage) or of 128 (plain (K, rows) maps with a zero-filled
+# tail), every padded M, both output types.
+SKINNY_SPLIT = [(16, 256, 16384, "f32"), (5, 384, 8320, "bf16"), (16, 512, 4000, "f32"),
+                (64, 1024, 8192, "bf16"), (128, 640, 4096, "f32"), (33, 4096, 2048, "bf16")]
+
+
+@pytest.mark.parametrize("M,N,K,out", SKINNY_SPLIT)
+def test_skinny_split_tiles(dev, oracle, M, N, K, out):
+    from gcnasm_b200 import ops
+    od = torch.bfloat16 if out == "bf16" else torch.float32
+    qa, sa, qb, sb = mx_operands(oracle, M, N, K)
+    ref = oracle.gemm_mx(qa, qb, sa, sb, M, N, K, acc_f64=True)
+    args = (T(qa, dev), T(qb, dev), T(oracle.sf_to_tc_layout(sa), dev), T(oracle.sf_to_tc_layout(sb), dev))
+    first = ops.mxfp8_gemm(*args, out_dtype=od)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    check_out(first, ref, od)
+    # the partials are added in segment order: a repeat is bit-identical, also
+    # after a call of another shape has used the same tile counters
+    qa2, sa2, qb2, sb2 = mx_operands(oracle, 7, 256, 8192, seed_a=11, seed_b=12)
+    ops.mxfp8_gemm(T(qa2, dev), T(qb2, dev), T(oracle.sf_to_tc_layout(sa2), dev),
+                   T(oracle.sf_to_tc_layout(sb2), dev), out_dtype=torch.float32)
+    again = ops.mxfp8_gemm(*args, out_dtype=od)
+    torch.cuda.synchronize()
+    assert torch.equal(first, again)
+
+
+def test_skinny_plain_fp8_split_tiles(dev, oracle):
+    """Plain FP8 (alpha only) on the skinny kernel, split tiles, bf16 out."""
+    from gcnasm_b200 import ops
+    M, N, K = 9, 384, 6144
+    qa, _ = oracle.quant_1x128(oracle.normal_rows(41, 0, M, K))  # E4M3 bytes; scales unused
+    qb, _ = oracle.quant_1x128(oracle.normal_rows(42, 0, N, K))
+    ref = oracle.gemm_a8w8(qa, qb, M, N, K).astype(np.float64) * 0.25
+    out = ops.gemm_a8w8(T(qa, dev), T(qb, dev), alpha=0.25, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    check_out(out, ref, torch.bfloat16)
+
+
+def test_skinny_cuda_graph_replay(dev, oracle):
+    """Decode loops replay captured launches: the tile counters are left at zero
+    by every launch, so each replay of the same captured launches (same counter
+    tag) recomputes the same bits."""
+    from gcnasm_b200 import ops
+    M, N, K = 16, 768, 8192  # 6 tiles over many CTAs: every tile split
+    qa, sa, qb, sb = mx_operands(oracle, M, N, K)
+    ref = oracle.gemm_mx(qa, qb, sa, sb, M, N, K, acc_f64=True)
+    args = (T(qa, dev), T(qb, dev), T(oracle.sf_to_tc_layout(sa), dev), T(oracle.sf_to_tc_layout(sb), dev))
+    out = torch.empty((M, N), dtype=torch.float32, device=dev)
+    eager = ops.mxfp8_gemm(*args, out_dtype=torch.float32)  # also the warm-up before capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        ops.mxfp8_gemm(*args, out=out)
+        ops.mxfp8_gemm(*args, out=out)
+    for _ in range(3):
+        out.fill_(float("nan"))
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, eager)
+    assert ops.device_status() == 0
+    check_out(out, ref, torch.float32)
