@@ -293,11 +293,20 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue: 4 warps, one TMEM lane group each
     // Columns are handled CH at a time so one CH-wide register array is live.
+    //
+    // A split tile's pieces p_0 .. p_{n-1} (segment order) are always added as
+    // the right fold p_0 + (p_1 + (... + p_{n-1})), whichever CTA finishes the
+    // tile, so the result does not depend on timing.  The CTA finishing a piece
+    // either finds (acquire load of the tile counter) that all other pieces are
+    // in -- then its own piece never leaves TMEM -- or stores its piece to its
+    // slot and counts in with a CAS; the arrival that completes the count adds.
     constexpr int CH = MP < 32 ? MP : 32;
+    constexpr bool kPreload = MP <= 32;  // others' pieces fit in registers ahead of the accumulator
     const int quad = warp & 3;
     const int r = quad * 32 + lane;  // TMEM lane = weight row in the tile = output column in the tile
     const int et = threadIdx.x - 64;
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
+    const int cta = static_cast<int>(blockIdx.x);
     int as = 0;
     uint32_t aph = 0;
     long long u = u_lo;
@@ -307,11 +316,37 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       const long long seg_end = u_hi < t0 + p.KG ? u_hi : t0 + p.KG;
       const int c0 = skinny_owner(t0, U, G), c1 = skinny_owner(t0 + p.KG - 1, U, G);
       const int nseg = c1 - c0 + 1;
-      // This CTA's last segment of a split tile finishes late, when the other
-      // segments' partials have long left L2: bring them back while its MMAs run.
-      if (nseg > 1 && seg_end == u_hi && et < nseg && c0 + et != static_cast<int>(blockIdx.x))
-        bulk_prefetch_l2(p.part + static_cast<long long>(skinny_slot(c0 + et, nt, U, G, p.KG)) * MP * 128,
-                         MP * 128 * 4);
+      const int j = cta - c0;  // this piece's index in the tile
+      const bool fin_seg = seg_end == u_hi;
+      unsigned long long* cnt = p.cnt + nt;
+      const unsigned long long all_others = (p.tag << 16) | static_cast<unsigned long long>(nseg - 1);
+      auto piece = [&](int jj) {  // this thread's column of piece jj's slot
+        return p.part + static_cast<long long>(skinny_slot(c0 + jj, nt, U, G, p.KG)) * MP * 128 + r;
+      };
+
+      // This CTA's last piece of a split tile usually finishes after the tile's
+      // other pieces: bring their slots into L2 while its MMAs run, and if they
+      // are all in already, fold the ones after it into registers now.
+      bool last = false, have_suffix = false;
+      float suffix[CH];
+      if (nseg > 1 && fin_seg) {
+        if (et < nseg && et != j) bulk_prefetch_l2(piece(et) - r, MP * 128 * 4);
+        if (et == 0) *last_flag = ld_acquire_gpu_u64(cnt) == all_others ? 1u : 0u;
+        skinny_epi_bar();
+        last = *last_flag != 0;
+        if (kPreload && last) {
+          for (int jj = nseg - 1; jj > j; --jj) {
+            const float* pj = piece(jj);
+            float y[CH];
+#pragma unroll
+            for (int i = 0; i < CH; ++i) y[i] = __ldcg(pj + i * 128);
+#pragma unroll
+            for (int i = 0; i < CH; ++i) suffix[i] = have_suffix ? y[i] + suffix[i] : y[i];
+            have_suffix = true;
+          }
+        }
+      }
+
       const bool got = mbar_wait(&acc_full[as], aph, abort_flag, p.status, kDevTimeoutEpilogue, tmo);
       if (!skinny_epi_all(got)) break;
       tc_fence_after();
@@ -341,6 +376,26 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
           tmem_ld_32x32b_x16(acc_addr + mc, *reinterpret_cast<uint32_t(*)[16]>(&x[0]));
         tc_wait_ld();
       };
+      // the right fold over pieces jj = hi .. 0 into t (rows [mc, mc + CH)), this
+      // CTA's piece taken from TMEM; t already holds the fold above hi if have_t
+      auto fold = [&](int mc, int hi, float (&t)[CH], bool have_t) {
+        for (int jj = hi; jj >= 0; --jj) {
+          float y[CH];
+          if (jj == j) {
+            uint32_t v[CH];
+            load_chunk(mc, v);
+#pragma unroll
+            for (int i = 0; i < CH; ++i) y[i] = __uint_as_float(v[i]);
+          } else {
+            const float* pj = piece(jj) + mc * 128;
+#pragma unroll
+            for (int i = 0; i < CH; ++i) y[i] = __ldcg(pj + i * 128);
+          }
+#pragma unroll
+          for (int i = 0; i < CH; ++i) t[i] = have_t ? y[i] + t[i] : y[i];
+          have_t = true;
+        }
+      };
 
       if (nseg == 1) {
 #pragma unroll 1
@@ -352,68 +407,58 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
           for (int i = 0; i < CH; ++i) x[i] = __uint_as_float(v[i]);
           store_out(mc, x);
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[as]);
       } else {
-        // Partial -> slot (first segment of this CTA: 2c, its last: 2c + 1); all
-        // MP rows, unpredicated, so the stores and the loads below pipeline.
-        const int slot = skinny_slot(static_cast<int>(blockIdx.x), nt, U, G, p.KG);
-        float* mine = p.part + static_cast<long long>(slot) * MP * 128 + r;
-#pragma unroll 1
-        for (int mc = 0; mc < MP; mc += CH) {
-          uint32_t v[CH];
-          load_chunk(mc, v);
-#pragma unroll
-          for (int i = 0; i < CH; ++i) __stcg(mine + (mc + i) * 128, __uint_as_float(v[i]));
+        if (fin_seg && !last) {  // look again now that this piece is done
+          if (et == 0) *last_flag = ld_acquire_gpu_u64(cnt) == all_others ? 1u : 0u;
+          skinny_epi_bar();
+          last = *last_flag != 0;
+          skinny_epi_bar();  // every thread has read the flag before it is written again
         }
-        // Count in: the barrier orders the four warps' stores before thread 0's
-        // release fence and arrival; its acquire fence and the second barrier
-        // order the reads of the other partials after the arrivals it saw.
-        skinny_epi_bar();
-        if (et == 0) {
-          fence_acq_rel_gpu();
-          // a CTA's last segment usually arrives after the tile's other pieces, its first before them
-          const int arrivals = skinny_arrive(p.cnt + nt, p.tag, seg_end == u_hi ? nseg - 1 : 0, p.status);
-          const bool last = arrivals == nseg;
-          if (last) fence_acq_rel_gpu();
-          *last_flag = last ? 1u : 0u;
-        }
-        skinny_epi_bar();
-        if (*last_flag != 0) {
-          // the partials added in segment order; this CTA's own comes from TMEM
-          // (the accumulator stage is released only after this)
+        if (!last) {
+          // store this piece (all MP rows, unpredicated, so stores and loads pipeline) and count in:
+          // the barrier orders the four warps' stores before thread 0's release fence and CAS; its
+          // acquire fence and the second barrier order the reads of the other pieces after it
+          float* mine = piece(j);
 #pragma unroll 1
           for (int mc = 0; mc < MP; mc += CH) {
-            float x[CH];
+            uint32_t v[CH];
+            load_chunk(mc, v);
 #pragma unroll
-            for (int i = 0; i < CH; ++i) x[i] = 0.f;
-            for (int jj = 0; jj < nseg; ++jj) {
-              const int cj = c0 + jj;
-              if (cj == static_cast<int>(blockIdx.x)) {
-                uint32_t v[CH];
-                load_chunk(mc, v);
-#pragma unroll
-                for (int i = 0; i < CH; ++i) x[i] += __uint_as_float(v[i]);
-              } else {
-                const float* pj = p.part + static_cast<long long>(skinny_slot(cj, nt, U, G, p.KG)) * MP * 128 +
-                                  mc * 128 + r;
-                float y[CH];
-#pragma unroll
-                for (int i = 0; i < CH; ++i) y[i] = __ldcg(pj + i * 128);
-#pragma unroll
-                for (int i = 0; i < CH; ++i) x[i] += y[i];
-              }
-            }
-            store_out(mc, x);
+            for (int i = 0; i < CH; ++i) __stcg(mine + (mc + i) * 128, __uint_as_float(v[i]));
           }
-          // all arrivals are in: leave the counter at zero for the next launch (or a replay)
-          if (et == 0) *reinterpret_cast<volatile unsigned long long*>(p.cnt + nt) = 0ull;
+          skinny_epi_bar();
+          if (et == 0) {
+            fence_acq_rel_gpu();
+            // a CTA's last piece usually arrives after the tile's other pieces, its first before them
+            const int arrivals = skinny_arrive(cnt, p.tag, fin_seg ? nseg - 1 : 0, p.status);
+            const bool done = arrivals == nseg;
+            if (done) fence_acq_rel_gpu();
+            *last_flag = done ? 1u : 0u;
+          }
+          skinny_epi_bar();
+          last = *last_flag != 0;
+          have_suffix = false;  // the fold below reads every other piece
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[as]);
+        if (last) {
+#pragma unroll 1
+          for (int mc = 0; mc < MP; mc += CH) {
+            float t[CH];
+            if (kPreload && have_suffix) {
+#pragma unroll
+              for (int i = 0; i < CH; ++i) t[i] = suffix[i];
+              fold(mc, j, t, true);
+            } else {
+              fold(mc, kPreload && fin_seg ? (have_suffix ? j : nseg - 1) : nseg - 1, t, false);
+            }
+            store_out(mc, t);
+          }
+          // every piece is in: leave the counter at zero for the next launch (or a replay)
+          if (et == 0) *reinterpret_cast<volatile unsigned long long*>(cnt) = 0ull;
+        }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[as]);
       if (++as == AS) { as = 0; aph ^= 1; }
       u = seg_end;
     }
