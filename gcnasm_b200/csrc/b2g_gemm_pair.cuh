@@ -20,7 +20,8 @@
 //     on both CTAs' `empty` / `acc_full` barriers;
 //   * both CTAs' epilogues drain their own TMEM and arrive on the leader's
 //     `acc_empty` (16 arrivals: 8 warps x 2 CTAs).
-// No TMA load uses .multicast::cluster and no kernel reads another GPU's memory.
+// Every TMA load targets its own CTA's shared memory (none is broadcast to the
+// cluster), and no kernel reads another GPU's memory.
 #pragma once
 
 #include "b2g_gemm.cuh"

@@ -348,8 +348,9 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 }
 
 // ---------------------------------------------------------------------------
-// CTA pairs (cluster of 2, tcgen05 cta_group::2).  No multicast TMA loads are
-// used anywhere; only tcgen05.commit multicasts its mbarrier arrival.
+// CTA pairs (cluster of 2, tcgen05 cta_group::2).  Each TMA load writes only
+// the issuing CTA's shared memory; only tcgen05.commit signals both CTAs'
+// barriers at once.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
