@@ -330,9 +330,11 @@ int dispatch_pre_out(const Env& d, bool pre, bool f32, const CUtensorMap& ta, co
 template <int kMode>
 int dispatch_bn(const Env& d, int bn, bool pre, bool f32, const CUtensorMap& ta, const CUtensorMap& tb,
                 const GemmParams& p, int grid, cudaStream_t st) {
-  // The blockwise mode keeps 128 fp32 sums per epilogue thread at kBN = 256,
-  // more than the 168-register budget of a 10-warp CTA; it runs 128-wide tiles.
-  if (kMode != kModeBlk && bn == 256) return dispatch_pre_out<kMode, 256>(d, pre, f32, ta, tb, p, grid, st);
+  // The blockwise mode runs 128-wide tiles only: it keeps 64 fp32 sums per epilogue
+  // thread at kBN = 128 (128 at kBN = 256, beyond the 168-register budget of a
+  // 10-warp CTA); no 256-wide blockwise kernel is compiled.
+  if constexpr (kMode != kModeBlk)
+    if (bn == 256) return dispatch_pre_out<kMode, 256>(d, pre, f32, ta, tb, p, grid, st);
   if (bn != 128) return fail(B2G_ERR_UNSUPPORTED, "no single-CTA kernel of width %d", bn);
   return dispatch_pre_out<kMode, 128>(d, pre, f32, ta, tb, p, grid, st);
 }

@@ -116,7 +116,9 @@ struct GemmCfg {
   // MMAs of block k still read)
   static constexpr int kSfCols = kMode == kModeMX ? 4 + 4 * kSfbAtoms : 0;
   static constexpr int kSfBufs = 2;
-  static constexpr int kAccStages = (kMode == kModeBlk) ? 2 : ((2 * kBN + kSfBufs * kSfCols <= 512) ? 2 : 1);
+  // blockwise: as many per-K-block partial buffers as TMEM holds, so the MMAs run
+  // up to three K blocks ahead of the promotion
+  static constexpr int kAccStages = (kMode == kModeBlk) ? 512 / kBN : ((2 * kBN + kSfBufs * kSfCols <= 512) ? 2 : 1);
   static constexpr int kSfaCol = kAccStages * kBN;  // + buffer * kSfCols
   static constexpr int kSfbCol = kSfaCol + 4;
   static constexpr int kTmemCols = 512;
@@ -361,23 +363,31 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
           if (!mbar_wait(&acc_full[as], aph, abort_flag, p.status, kDevTimeoutEpilogue, tmo)) { ok = false; break; }
           tc_fence_after();
           const float s_const = sa * __shfl_sync(0xffffffffu, sb.x, 0);
+          // the K block's partial in 32-column groups, one wait per group (64 columns
+          // at once would exceed the 168-register budget of a 10-warp CTA)
+          constexpr int KBLK = 32;
 #pragma unroll
-          for (int c = 0; c < NC / 16; ++c) {  // 16-column loads keep the register budget (168) spill-free
-            uint32_t v[16];
-            tmem_ld_32x32b_x16(tmem_base + lane_addr + as * kBN + half * NC + c * 16, v);
+          for (int c = 0; c < NC / KBLK; ++c) {
+            uint32_t v[KBLK];
+#pragma unroll
+            for (int q = 0; q < KBLK / 16; ++q)
+              tmem_ld_32x32b_x16(tmem_base + lane_addr + as * kBN + half * NC + c * KBLK + q * 16,
+                                 *reinterpret_cast<uint32_t(*)[16]>(&v[q * 16]));
             tc_wait_ld();
             if (gn1) {
 #pragma unroll
-              for (int j = 0; j < 16; j += 4) {
-                const float4 b4 = *reinterpret_cast<const float4*>(sb_stage + c * 16 + j);
-                acc[c * 16 + j + 0] = fmaf(__uint_as_float(v[j + 0]) * b4.x, sa, acc[c * 16 + j + 0]);
-                acc[c * 16 + j + 1] = fmaf(__uint_as_float(v[j + 1]) * b4.y, sa, acc[c * 16 + j + 1]);
-                acc[c * 16 + j + 2] = fmaf(__uint_as_float(v[j + 2]) * b4.z, sa, acc[c * 16 + j + 2]);
-                acc[c * 16 + j + 3] = fmaf(__uint_as_float(v[j + 3]) * b4.w, sa, acc[c * 16 + j + 3]);
+              for (int j = 0; j < KBLK; j += 4) {
+                const float4 b4 = *reinterpret_cast<const float4*>(sb_stage + c * KBLK + j);
+                fmul_ffma2(acc[c * KBLK + j + 0], acc[c * KBLK + j + 1], __uint_as_float(v[j + 0]),
+                           __uint_as_float(v[j + 1]), b4.x, b4.y, sa);
+                fmul_ffma2(acc[c * KBLK + j + 2], acc[c * KBLK + j + 3], __uint_as_float(v[j + 2]),
+                           __uint_as_float(v[j + 3]), b4.z, b4.w, sa);
               }
             } else {
 #pragma unroll
-              for (int j = 0; j < 16; ++j) acc[c * 16 + j] = fmaf(__uint_as_float(v[j]), s_const, acc[c * 16 + j]);
+              for (int j = 0; j < KBLK; j += 2)
+                ffma2_bcast(acc[c * KBLK + j], acc[c * KBLK + j + 1], __uint_as_float(v[j]),
+                            __uint_as_float(v[j + 1]), s_const);
             }
           }
           tc_fence_before();

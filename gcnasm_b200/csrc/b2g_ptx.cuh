@@ -149,6 +149,25 @@ __device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* m, uin
       : "memory");
 }
 
+// Packed two-wide fp32 arithmetic (one instruction for two lanes of work, each
+// rounded exactly as the scalar fmaf / multiply):
+//   (c0, c1) = (a0 * b + c0, a1 * b + c1)
+__device__ __forceinline__ void ffma2_bcast(float& c0, float& c1, float a0, float a1, float b) {
+  asm("{\n\t.reg .b64 ra, rb, rc;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %4};\n\tmov.b64 rc, {%0, %1};\n\t"
+      "fma.rn.f32x2 rc, ra, rb, rc;\n\tmov.b64 {%0, %1}, rc;\n\t}"
+      : "+f"(c0), "+f"(c1)
+      : "f"(a0), "f"(a1), "f"(b));
+}
+//   (c0, c1) = ((a0 * b0) * s + c0, (a1 * b1) * s + c1)
+__device__ __forceinline__ void fmul_ffma2(float& c0, float& c1, float a0, float a1, float b0, float b1, float s) {
+  asm("{\n\t.reg .b64 ra, rb, rs, rc;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rs, {%6, %6};\n\tmov.b64 rc, {%0, %1};\n\t"
+      "mul.rn.f32x2 ra, ra, rb;\n\tfma.rn.f32x2 rc, ra, rs, rc;\n\tmov.b64 {%0, %1}, rc;\n\t}"
+      : "+f"(c0), "+f"(c1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(s));
+}
+
 // 1-D bulk copy; src and dst 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
