@@ -23,6 +23,7 @@
 #include "b2g_gemm.cuh"
 #include "b2g_gemm_pair.cuh"
 #include "b2g_gemm_skinny.cuh"
+#include "b2g_gemm_skinny_blk.cuh"
 
 using namespace b2g;
 
@@ -427,12 +428,21 @@ int plan_tiles(const Req& r, int sms, int* bn_out, int* S_out, int* kb_per_out, 
 }
 
 // Few rows of A (decode): the transposed stream-K kernel.
-bool use_skinny(const Req& r) {
+bool use_skinny(const Req& r, int sms) {
   static const bool off = [] {
     const char* v = getenv("B2G_DISABLE_SKINNY");
     return v && v[0] == '1';
   }();
-  return !off && r.M <= 128 && r.batch == 1 && r.mode != kModeBlk && cdiv(r.N, 128) <= kSkinnyMaxTiles;
+  if (off || r.M > 128 || r.batch != 1 || cdiv(r.N, 128) > kSkinnyMaxTiles) return false;
+  // The blockwise decode kernel folds every K block's partial into registers, one
+  // 32-column TMEM load at a time.  Measured against the single-CTA kernel it wins
+  // only for at most 32 rows of A and more 128-row tiles than SMs (the single-CTA
+  // kernel then needs a second, partial wave).  It TMA-loads the scale rows, which
+  // must start on 16 bytes.
+  if (r.mode == kModeBlk)
+    return r.M <= 32 && cdiv(r.N, 128) > sms && r.stride_sfa % 4 == 0 && aligned16(r.bsa) &&
+           (r.group_n == 1 || (r.stride_sfb % 4 == 0 && aligned16(r.bsb)));
+  return true;
 }
 
 // B2G_DISABLE_PDL=1 launches without programmatic stream serialization.
@@ -456,7 +466,7 @@ long long skinny_units(const Req& r) {
 
 // Scratch bytes run_gemm will ask for beyond r.ws_offset.
 size_t split_ws_bytes(const Req& r, int S, int sms) {
-  if (use_skinny(r)) {  // fp32 partial slots, two per CTA
+  if (use_skinny(r, sms)) {  // fp32 partial slots, two per CTA
     const long long grid = std::min<long long>(skinny_units(r), sms);
     return static_cast<size_t>(2 * grid) * skinny_mp(r.M) * 128 * 4;
   }
@@ -483,6 +493,44 @@ int launch_skinny(const Env& d, const CUtensorMap& tw, const CUtensorMap& ta, co
   cfg.numAttrs = 1;
   B2G_CUDA(cudaLaunchKernelEx(&cfg, b2g_gemm_skinny_kernel<Cfg>, tw, ta, sp));
   return B2G_OK;
+}
+
+template <class Cfg>
+int launch_skinny_blk(const Env& d, const CUtensorMap& tw, const CUtensorMap& ta, const CUtensorMap& tsa,
+                      const CUtensorMap& tsb, const SkinnyParams& sp, int grid, cudaStream_t st) {
+  const void* fn = reinterpret_cast<const void*>(&b2g_gemm_skinny_blk_kernel<Cfg>);
+  int rc = ensure_smem_attr(d.fns, fn, Cfg::kSmemBytes);
+  if (rc) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(Cfg::kThreads);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = use_pdl() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  B2G_CUDA(cudaLaunchKernelEx(&cfg, b2g_gemm_skinny_blk_kernel<Cfg>, tw, ta, tsa, tsb, sp));
+  return B2G_OK;
+}
+
+int dispatch_skinny_blk(const Env& d, int mp, int kkb, const CUtensorMap& tw, const CUtensorMap& ta,
+                        const CUtensorMap& tsa, const CUtensorMap& tsb, const SkinnyParams& sp, int grid,
+                        cudaStream_t st) {
+  if (kkb == 2) {
+    switch (mp) {
+      case 16: return launch_skinny_blk<SkinnyBlkCfg<16, 2>>(d, tw, ta, tsa, tsb, sp, grid, st);
+      case 32: return launch_skinny_blk<SkinnyBlkCfg<32, 2>>(d, tw, ta, tsa, tsb, sp, grid, st);
+      default: return launch_skinny_blk<SkinnyBlkCfg<64, 2>>(d, tw, ta, tsa, tsb, sp, grid, st);
+    }
+  }
+  switch (mp) {
+    case 16: return launch_skinny_blk<SkinnyBlkCfg<16, 1>>(d, tw, ta, tsa, tsb, sp, grid, st);
+    case 32: return launch_skinny_blk<SkinnyBlkCfg<32, 1>>(d, tw, ta, tsa, tsb, sp, grid, st);
+    case 64: return launch_skinny_blk<SkinnyBlkCfg<64, 1>>(d, tw, ta, tsa, tsb, sp, grid, st);
+    default: return launch_skinny_blk<SkinnyBlkCfg<128, 1>>(d, tw, ta, tsa, tsb, sp, grid, st);
+  }
 }
 
 template <int kMode, bool kPre>
@@ -529,6 +577,11 @@ int run_skinny(const Req& r, const Env& d) {
   sp.status = d.status;
   sp.timeout_ns = g_timeout_ns.load();
   sp.debug_stall = g_force_stall.load();
+  sp.bsa = r.bsa;
+  sp.bsb = r.bsb;
+  sp.stride_sfa = r.stride_sfa;
+  sp.stride_sfb = r.stride_sfb;
+  sp.group_n = r.group_n;
 
   // Operand maps.  With K % 128 == 0 they view a row-major [rows][K] operand as
   // (128 bytes, rows, K/128 blocks) so one box brings kkb whole K blocks, each
@@ -573,7 +626,33 @@ int run_skinny(const Req& r, const Env& d) {
   rc = env_workspace(d, r.ws_offset + split_ws_bytes(r, 1, d.sms), &ws);
   if (rc) return rc;
   sp.part = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + r.ws_offset);
-  if (r.mode == kModeMX)
+  if (r.mode == kModeBlk) {
+    // fp32 scale rows as 2-D TMA boxes: sfa (MP rows of one K block); sfb the tile's
+    // 128 column scales (GROUP_N = 1) or 8 block scales around the K block (GROUP_N = 128)
+    CUtensorMap tsa, tsb;
+    const long long kbt = r.K / 128;
+    {
+      cuuint64_t dims[2] = {(cuuint64_t)r.M, (cuuint64_t)kbt};
+      cuuint64_t str[1] = {(cuuint64_t)(r.stride_sfa * 4)};
+      cuuint32_t box[2] = {(cuuint32_t)mp, 1};
+      rc = encode(&tsa, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, r.bsa, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+      if (rc) return rc;
+    }
+    if (r.group_n == 1) {
+      cuuint64_t dims[2] = {(cuuint64_t)r.N, (cuuint64_t)kbt};
+      cuuint64_t str[1] = {(cuuint64_t)(r.stride_sfb * 4)};
+      cuuint32_t box[2] = {128, 1};
+      rc = encode(&tsb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, r.bsb, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+    } else {
+      cuuint64_t dims[2] = {(cuuint64_t)kbt, (cuuint64_t)(r.N / 128)};
+      cuuint64_t str[1] = {(cuuint64_t)(r.stride_sfb * 4)};
+      cuuint32_t box[2] = {8, 1};
+      rc = encode(&tsb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, r.bsb, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+    }
+    if (rc) return rc;
+    rc = dispatch_skinny_blk(d, mp, kkb, tw, ta, tsa, tsb, sp, grid, r.stream);
+  }
+  else if (r.mode == kModeMX)
     rc = r.bpre ? dispatch_skinny_mp<kModeMX, true>(d, mp, kkb, tw, ta, sp, grid, r.stream)
                 : dispatch_skinny_mp<kModeMX, false>(d, mp, kkb, tw, ta, sp, grid, r.stream);
   else
@@ -624,7 +703,7 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
     env = env_of(dst);
   }
   const Env& d = env;
-  if (use_skinny(r)) return run_skinny(r, d);
+  if (use_skinny(r, d.sms)) return run_skinny(r, d);
 
   // ---- tile + split
   int bn = 0, S = 1, kb_per = 1, bm = 128;

@@ -73,6 +73,12 @@ struct SkinnyParams {
   const uint8_t* sfw;  // weight (B) scales, tensor-core atom layout, atoms [n_block][k_block]
   const uint8_t* sfa;  // activation (A) scales, same layout (one row block)
   long long sf_rb;     // bytes between row blocks of either scale buffer
+  // fp32 block scales (b2g_gemm_skinny_blk_kernel): bsa [K/128][stride_sfa] per row of A;
+  // bsb [N/128][stride_sfb] per 128x128 block (group_n 128) or [K/128][stride_sfb] per column (1)
+  const float* bsa;
+  const float* bsb;
+  long long stride_sfa, stride_sfb;
+  int group_n;
   int NT, KG;          // 128-row weight tiles; K groups (kKB blocks each) per tile
   int kview;           // 1: operand maps are (128, rows, K/128) views, coordinates (0, row, k_block);
                        // 0: (K, rows, 1) maps, coordinates (k_block * 128, row, 0)

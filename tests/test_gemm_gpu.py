@@ -479,3 +479,34 @@ def test_skinny_cuda_graph_replay(dev, oracle):
         assert torch.equal(out, eager)
     assert ops.device_status() == 0
     check_out(out, ref, torch.float32)
+
+
+# Blockwise scales with M <= 32 rows and more 128-row tiles than SMs run on the
+# stream-K decode kernel that folds each 128-K block into registers (M=16/32: one
+# or two K blocks per stage, split tiles, both scale layouts, both output types);
+# M=7 (scale rows not 16-byte aligned) and the smaller shapes exercise the
+# single-CTA kernel's small-M path.
+SKINNY_BLK = [(16, 19200, 1536, 128, "f32"), (12, 19328, 2048, 128, "bf16"), (16, 19456, 640, 1, "bf16"),
+              (32, 19200, 1280, 1, "f32"), (7, 19200, 768, 128, "bf16"), (1, 256, 8192, 128, "f32"),
+              (64, 384, 6144, 1, "f32"), (128, 7168, 2048, 128, "bf16")]
+
+
+@pytest.mark.parametrize("M,N,K,group_n,out", SKINNY_BLK)
+def test_blockscale_skinny(dev, oracle, M, N, K, group_n, out):
+    from gcnasm_b200 import ops
+    od = torch.bfloat16 if out == "bf16" else torch.float32
+    qa, sfa = oracle.quant_1x128(oracle.normal_rows(71, 0, M, K))
+    if group_n == 128:
+        qb, sfb = oracle.quant_128x128(oracle.normal_rows(72, 0, N, K))
+        ref = oracle.gemm_blockscale_f64(qa, qb, sfa, sfb, M, N, K, M, K // 128, 128, 0)
+    else:
+        qb, sfb = oracle.quant_1x128(oracle.normal_rows(72, 0, N, K))  # [K/128, N]
+        ref = oracle.gemm_blockscale_f64(qa, qb, sfa, sfb, M, N, K, M, N, 1, 1)
+    args = (T(qa, dev), T(qb, dev), T(sfa, dev), T(sfb, dev))
+    first = ops.gemm_a8w8_blockscale(*args, group_n=group_n, out_dtype=od)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    check_out(first, ref, od)
+    again = ops.gemm_a8w8_blockscale(*args, group_n=group_n, out_dtype=od)
+    torch.cuda.synchronize()
+    assert torch.equal(first, again)
