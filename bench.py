@@ -228,6 +228,9 @@ def run_b200(args, rank, world, local_rank):
         "clocks": clk,
         "gpu_launches": args.steps,
     }
+    # ---------------------------------------------------------------- C5: the 8-GPU sharded config
+    c5 = bench_c5(args, dev, stream, world, rank, flush)
+
     # ---------------------------------------------------------------- e2e through the f4gemm C-ABI
     # every rank runs its shard through the reference-facing call; the job's
     # time per step is the slowest rank's
@@ -242,6 +245,7 @@ def run_b200(args, rank, world, local_rank):
     if rank != 0:
         return None
     result["e2e"] = e2e
+    result["c5"] = c5
 
     # ---------------------------------------------------------------- decode config (HBM-bound)
     result["decode"] = bench_decode(args, dev, stream, peaks, flush)
@@ -253,6 +257,86 @@ def run_b200(args, rank, world, local_rank):
                                             "accumulate, OpenMP over rows; extrapolates linearly in M)"}
     del capi, f4gemm
     return result
+
+
+def bench_c5(args, dev, stream, world, rank, flush):
+    """The sharded config (C5): MXFP8 M=65536, N=28672, K=8192, bf16 C, over the
+    job's GPUs.  M-shard: rank g computes its 65536/N rows with B replicated, no
+    collective (strong scaling of the fixed problem).  At N > 1 also the
+    column-parallel form: A replicated, rank g computes C[:, its 28672/N columns]
+    and the bf16 slabs are all-gathered over NCCL into the full C on every rank
+    (gcnasm_b200.shard).  Device time per step, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from gcnasm_b200 import ops, shard
+
+    M, N, K = 65536, 28672, 8192
+    steps = max(3, min(args.steps, 10))
+
+    def max_over_ranks(ms):
+        t = torch.tensor([ms], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- M-shard
+    row0, rows = shard.row_range(M, world, rank)
+    g = torch.Generator(device=dev)
+    x = torch.randn(rows, K, device=dev, generator=g.manual_seed(500 + rank))
+    qa, sfa = ops.quant_mxfp8(x, "tc")
+    del x
+    w = torch.randn(N, K, device=dev, generator=g.manual_seed(501))  # the same B on every rank
+    qb, sfb = ops.quant_mxfp8(w, "tc")
+    del w
+    out = torch.empty((rows, N), dtype=torch.bfloat16, device=dev)
+
+    def step_m():
+        ops.mxfp8_gemm(qa, qb, sfa, sfb, out=out, stream=stream)
+
+    step_m()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = max_over_ranks(sum(timed_steps(step_m, steps, 3, flush, stream)) / steps)
+    res = {"M": M, "N": N, "K": K, "out": "bf16", "steps": steps,
+           "m_shard": {"value": round(2.0 * M * N * K / (ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                       "ms_per_step": round(ms, 3), "rows_per_gpu": rows, "n_gpus": world,
+                       "scaling": "strong (fixed 65536-row problem)", "collective": "none"}}
+    del qa, sfa, out
+    torch.cuda.empty_cache()
+
+    # ---- N-shard + NCCL all-gather of C
+    if world > 1:
+        assert N % (128 * world) == 0
+        col0, cols = shard.col_range(N, world, rank)
+        x = torch.randn(M, K, device=dev, generator=g.manual_seed(502))  # the same A on every rank
+        qa, sfa = ops.quant_mxfp8(x, "tc")
+        del x
+        qb_local = qb[col0:col0 + cols]
+        sfb_local = sfb[shard.sf_tc_row_offset(col0, K):shard.sf_tc_row_offset(col0 + cols, K)]
+        c_local = torch.empty((M, cols), dtype=torch.bfloat16, device=dev)
+
+        def local_gemm(c0, nc):
+            ops.mxfp8_gemm(qa, qb_local, sfa, sfb_local, out=c_local, stream=stream)
+            return c_local
+
+        def step_n():
+            shard.n_sharded_allgather(local_gemm, N, world, rank)
+
+        step_n()
+        torch.cuda.synchronize()
+        dist.barrier()
+        ms_n = max_over_ranks(sum(timed_steps(step_n, steps, 3, flush, stream)) / steps)
+        res["n_shard_allgather"] = {
+            "value": round(2.0 * M * N * K / (ms_n * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+            "ms_per_step": round(ms_n, 3), "cols_per_gpu": cols, "n_gpus": world,
+            "collective": "NCCL all_gather of the bf16 column slabs (M x N/world x 2 B per rank), then the "
+                          "[M, N] assembly, inside the timed step"}
+        del qa, sfa, c_local
+    del qb, sfb
+    torch.cuda.empty_cache()
+    return res
 
 
 def bench_decode(args, dev, stream, peaks, flush):
