@@ -740,6 +740,21 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
   else if (r.out_f32) p.out_mode = kOutAtomic;
   else p.out_mode = kOutWorkspace;
 
+  // C through TMA stores when its row pitch (and batch stride) are whole 16 bytes
+  {
+    const long long es = r.out_f32 ? 4 : 2;
+    const long long bstride = r.batch > 1 ? r.c_bstride : r.ldc * r.M;
+    if (p.out_mode == kOutStore && (r.ldc * es) % 16 == 0 && (bstride * es) % 16 == 0) {
+      cuuint64_t dims[3] = {(cuuint64_t)r.N, (cuuint64_t)r.M, (cuuint64_t)r.batch};
+      cuuint64_t str[2] = {(cuuint64_t)(r.ldc * es), (cuuint64_t)(bstride * es)};
+      cuuint32_t box[3] = {(cuuint32_t)(64 / es), 32, 1};
+      rc = encode(&p.tm_c, r.out_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, r.c,
+                  dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+      if (rc) return rc;
+      p.tma_store = 1;
+    }
+  }
+
   // ---- tensor maps
   CUtensorMap ta, tb;
   {

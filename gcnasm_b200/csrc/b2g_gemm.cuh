@@ -39,6 +39,11 @@ enum Mode : int { kModePlain = 0, kModeMX = 1, kModeBlk = 2 };
 enum OutMode : int { kOutStore = 0, kOutAtomic = 1, kOutWorkspace = 2 };
 
 struct GemmParams {
+  // C as a (N, M, batch) TMA map with (64 bytes of columns) x 32 rows boxes; used
+  // when tma_store is set (plain stores, 16-byte row pitch), else C is written
+  // with vector stores
+  CUtensorMap tm_c;
+  int tma_store;
   int M, N, K, batch;
   // output: C[b][m][n] at c + b*c_bstride + m*ldc + n (elements of the output type)
   void* c;
@@ -70,6 +75,44 @@ struct GemmParams {
 struct Unit {
   int b, mt, nt, ks, kb0, kb1;
 };
+
+// Epilogue write through TMA: this warp's 32 rows (row0 + lane) x NC columns
+// (col0 + j, values acc[j] of the lane's row) of C, converted to the output type
+// and staged 64 bytes of columns at a time in the warp's 2 KB of shared memory,
+// each chunk a (64 B x 32 rows) box stored by lane 0.  Rows past M and columns
+// past N are clipped by the store itself, so every lane takes part.
+template <int NC, bool kF32>
+__device__ __forceinline__ void tma_store_rows(const CUtensorMap* tm, const float (&acc)[NC], int col0, int row0,
+                                               int b, uint8_t* stage, int lane) {
+  constexpr int CH = kF32 ? 16 : 32;  // columns per 64-byte row chunk
+  uint4* mine = reinterpret_cast<uint4*>(stage + lane * 64);
+#pragma unroll
+  for (int c = 0; c < NC / CH; ++c) {
+    if (c > 0) {  // the previous chunk's store has read the stage
+      if (lane == 0) bulk_wait_read_all();
+      __syncwarp();
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      if (kF32)
+        mine[q] = make_uint4(__float_as_uint(acc[c * CH + 4 * q]), __float_as_uint(acc[c * CH + 4 * q + 1]),
+                             __float_as_uint(acc[c * CH + 4 * q + 2]), __float_as_uint(acc[c * CH + 4 * q + 3]));
+      else
+        mine[q] = make_uint4(pack_bf16x2(acc[c * CH + 8 * q], acc[c * CH + 8 * q + 1]),
+                             pack_bf16x2(acc[c * CH + 8 * q + 2], acc[c * CH + 8 * q + 3]),
+                             pack_bf16x2(acc[c * CH + 8 * q + 4], acc[c * CH + 8 * q + 5]),
+                             pack_bf16x2(acc[c * CH + 8 * q + 6], acc[c * CH + 8 * q + 7]));
+    }
+    fence_proxy_async_smem();  // the generic-proxy writes above, visible to the TMA
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_3d(tm, stage, col0 + c * CH, row0, b);
+      bulk_commit_group();
+    }
+  }
+  if (lane == 0) bulk_wait_read_all();  // the stage is free for the next tile
+  __syncwarp();
+}
 
 __host__ __device__ __forceinline__ Unit decode_unit(int u, const GemmParams& p) {
   Unit w;
@@ -130,7 +173,9 @@ struct GemmCfg {
   static constexpr int kOffSfb = kOffSfa + kStages * kSfaBytes;
   static constexpr int kOffSbStage = kOffSfb + kStages * kSfbBytes;  // GROUP_N=1 column scales
   static constexpr int kSbStageBytes = kMode == kModeBlk ? kEpiWarps * kColsPerThread * 4 : 0;
-  static constexpr int kOffBar = (kOffSbStage + kSbStageBytes + 7) / 8 * 8;
+  static constexpr int kOffStageC = (kOffSbStage + kSbStageBytes + 1023) / 1024 * 1024;  // TMA-store staging
+  static constexpr int kStageCBytes = kEpiWarps * 2048;                                     // 2 KB per warp
+  static constexpr int kOffBar = (kOffStageC + kStageCBytes + 7) / 8 * 8;
   static constexpr int kNumBars = 2 * kStages + 2 * kAccStages + 2;
   static constexpr int kOffCtl = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffCtl + 16 + 1024;  // + alignment slack
@@ -304,6 +349,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     int as = 0;
     uint32_t aph = 0;
     float* sb_stage = reinterpret_cast<float*>(smem + Cfg::kOffSbStage) + ew * NC;
+    uint8_t* stage_c = smem + Cfg::kOffStageC + ew * 2048;
 
     for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
       const Unit w = decode_unit(u, p);
@@ -399,7 +445,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       }
 
       // ---- write the row segment [col0, col0 + NC) of row m
-      if (m < p.M) {
+      if (p.tma_store && p.out_mode == kOutStore) {
+        tma_store_rows<NC, Cfg::kOutF32>(&p.tm_c, acc, col0, w.mt * 128 + quad * 32, w.b, stage_c, lane);
+      } else if (m < p.M) {
         if (p.out_mode == kOutWorkspace) {
           float* dst = p.ws + ((static_cast<long long>(w.ks) * p.batch + w.b) * p.M + m) * static_cast<long long>(p.N);
 #pragma unroll
@@ -430,6 +478,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         }
       }
     }
+    if (lane == 0) bulk_wait_all();  // this warp's TMA stores of C are complete
   }
 
   // ------------------------------------------------------------ teardown

@@ -65,7 +65,9 @@ struct PairCfg {
   static constexpr int kOffB = kOffA + kStages * kABytes;
   static constexpr int kOffSfa = kOffB + kStages * kBBytes;
   static constexpr int kOffSfb = kOffSfa + kStages * kSfaBytes;
-  static constexpr int kOffBar = (kOffSfb + kStages * kSfbBytes + 7) / 8 * 8;
+  static constexpr int kOffStageC = (kOffSfb + kStages * kSfbBytes + 1023) / 1024 * 1024;  // TMA-store staging
+  static constexpr int kStageCBytes = kEpiWarps * 2048;                                        // 2 KB per warp
+  static constexpr int kOffBar = (kOffStageC + kStageCBytes + 7) / 8 * 8;
   static constexpr int kNumBars = 2 * kStages + 2 * kAccStages + 2;
   static constexpr int kOffCtl = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffCtl + 16 + 1024;
@@ -234,6 +236,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     const int row_in_tile = static_cast<int>(rank) * 128 + quad * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
     constexpr int NC = Cfg::kColsPerThread;
+    uint8_t* stage_c = smem + Cfg::kOffStageC + ew * 2048;
     int as = 0;
     uint32_t aph = 0;
     for (int u = pair; u < p.num_units; u += pp.num_pairs) {
@@ -256,7 +259,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       float acc[NC];
 #pragma unroll
       for (int j = 0; j < NC; ++j) acc[j] = __uint_as_float(v[j]) * p.alpha;
-      if (m < p.M) {
+      if (p.tma_store && p.out_mode == kOutStore) {
+        tma_store_rows<NC, Cfg::kOutF32>(&p.tm_c, acc, col0, w.mt * 256 + static_cast<int>(rank) * 128 + quad * 32, w.b, stage_c, lane);
+      } else if (m < p.M) {
         if (p.out_mode == kOutWorkspace) {
           float* dst = p.ws + ((static_cast<long long>(w.ks) * p.batch + w.b) * p.M + m) * static_cast<long long>(p.N);
 #pragma unroll
@@ -287,6 +292,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         }
       }
     }
+    if (lane == 0) bulk_wait_all();  // this warp's TMA stores of C are complete
   }
 
   // ------------------------------------------------------------ teardown
