@@ -333,7 +333,28 @@ def bench_c5(args, dev, stream, world, rank, flush):
             "ms_per_step": round(ms_n, 3), "cols_per_gpu": cols, "n_gpus": world,
             "collective": "NCCL all_gather of the bf16 column slabs (M x N/world x 2 B per rank), then the "
                           "[M, N] assembly, inside the timed step"}
-        del qa, sfa, c_local
+        del c_local
+        torch.cuda.empty_cache()
+
+        # the same with the gather folded into the GEMM epilogue (peer stores over NVLink)
+        c_full, ptrs = shard.peer_output(M, N, torch.bfloat16)
+        barrier = torch.zeros(1, device=dev)
+
+        def step_p():
+            shard.n_sharded_peer_out(qa, sfa, qb_local, sfb_local, c_full, ptrs, N, world, rank, barrier)
+
+        step_p()
+        torch.cuda.synchronize()
+        dist.barrier()
+        ms_p = max_over_ranks(sum(timed_steps(step_p, steps, 3, flush, stream)) / steps)
+        res["n_shard_peer_out"] = {
+            "value": round(2.0 * M * N * K / (ms_p * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+            "ms_per_step": round(ms_p, 3), "cols_per_gpu": cols, "n_gpus": world,
+            "collective": "none on the data path: each GPU's GEMM epilogue stores its columns into every "
+                          "GPU's full C (symmetric memory, NVLink); a one-element NCCL all-reduce orders the "
+                          "ranks, inside the timed step"}
+        dist.barrier()
+        del qa, sfa, c_full
     del qb, sfb
     torch.cuda.empty_cache()
     return res

@@ -300,6 +300,10 @@ struct Req {
   int log2_k_split = 0;
   size_t ws_offset = 0;  // scratch bytes already claimed by the caller of run_gemm
   cudaStream_t stream = nullptr;
+  // column-parallel output into every GPU's full C (b2g_gemm_mxfp8_peer_out)
+  void* const* peer_c = nullptr;
+  int n_peers = 0, peer_self = 0;
+  long long peer_ldc = 0, peer_col0 = 0;
 };
 
 template <class Cfg>
@@ -433,7 +437,7 @@ bool use_skinny(const Req& r, int sms) {
     const char* v = getenv("B2G_DISABLE_SKINNY");
     return v && v[0] == '1';
   }();
-  if (off || r.M > 128 || r.batch != 1 || cdiv(r.N, 128) > kSkinnyMaxTiles) return false;
+  if (off || r.M > 128 || r.batch != 1 || r.n_peers || cdiv(r.N, 128) > kSkinnyMaxTiles) return false;
   // The blockwise decode kernel folds every K block's partial into registers, one
   // 32-column TMEM load at a time.  Measured against the single-CTA kernel it wins
   // only for at most 32 rows of A and more 128-row tiles than SMs (the single-CTA
@@ -736,9 +740,21 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
   p.timeout_ns = g_timeout_ns.load();
   p.debug_stall = g_force_stall.load();
 
-  if (S == 1) p.out_mode = kOutStore;
-  else if (r.out_f32) p.out_mode = kOutAtomic;
-  else p.out_mode = kOutWorkspace;
+  if (r.n_peers) {
+    if (S != 1) return fail(B2G_ERR_UNSUPPORTED, "the peer-store output takes no K split");
+    p.out_mode = kOutPeers;
+    for (int i = 0; i < r.n_peers; ++i) p.peer_c[i] = r.peer_c[i];
+    p.n_peers = r.n_peers;
+    p.peer_first = r.peer_self;
+    p.peer_ldc = r.peer_ldc;
+    p.peer_col0 = r.peer_col0;
+  } else if (S == 1) {
+    p.out_mode = kOutStore;
+  } else if (r.out_f32) {
+    p.out_mode = kOutAtomic;
+  } else {
+    p.out_mode = kOutWorkspace;
+  }
 
   // C through TMA stores when its row pitch (and batch stride) are whole 16 bytes
   {
@@ -1036,6 +1052,41 @@ int b2g_gemm_mxfp8(const b2g_mxfp8_args* g, void* stream) {
   r.sfb = static_cast<const uint8_t*>(g->sfb);
   r.log2_k_split = g->log2_k_split;
   r.stream = static_cast<cudaStream_t>(stream);
+  return run_gemm(r);
+}
+
+int b2g_gemm_mxfp8_peer_out(const b2g_mxfp8_args* g, void* const* peer_d, int n_peers, int self,
+                            long long ldd_full, long long col_offset, void* stream) {
+  if (!g || !peer_d) return fail(B2G_ERR_INVALID_ARG, "null args");
+  if (g->out_dtype != B2G_OUT_BF16 && g->out_dtype != B2G_OUT_F32) return fail(B2G_ERR_INVALID_ARG, "bad out_dtype");
+  if (n_peers < 1 || n_peers > kMaxPeers) return fail(B2G_ERR_INVALID_ARG, "n_peers must be 1..%d", kMaxPeers);
+  if (self < 0 || self >= n_peers) return fail(B2G_ERR_INVALID_ARG, "self %d outside 0..%d", self, n_peers - 1);
+  const long long es = g->out_dtype == B2G_OUT_F32 ? 4 : 2;
+  for (int i = 0; i < n_peers; ++i)
+    if (!peer_d[i] || !aligned16(peer_d[i])) return fail(B2G_ERR_ALIGNMENT, "peer buffer %d null or not 16-byte aligned", i);
+  if (col_offset < 0 || ldd_full < col_offset + g->n)
+    return fail(B2G_ERR_INVALID_ARG, "columns [%lld, %lld) outside the %lld-column peer buffers", col_offset,
+                col_offset + g->n, ldd_full);
+  if ((ldd_full * es) % 16 || (col_offset * es) % 16)
+    return fail(B2G_ERR_ALIGNMENT, "peer row pitch and column offset must be whole 16 bytes");
+  Req r;
+  r.mode = kModeMX;
+  r.bpre = g->b_preshuffled != 0;
+  r.out_f32 = g->out_dtype == B2G_OUT_F32;
+  r.M = g->m; r.N = g->n; r.K = g->k;
+  r.a = g->a; r.lda = g->lda;
+  r.b = g->b; r.ldb = r.bpre ? g->k : g->ldb;
+  r.c = peer_d[self]; r.ldc = ldd_full;
+  r.alpha = g->alpha;
+  r.sfa = static_cast<const uint8_t*>(g->sfa);
+  r.sfb = static_cast<const uint8_t*>(g->sfb);
+  r.log2_k_split = 0;
+  r.stream = static_cast<cudaStream_t>(stream);
+  r.peer_c = peer_d;
+  r.n_peers = n_peers;
+  r.peer_self = self;
+  r.peer_ldc = ldd_full;
+  r.peer_col0 = col_offset;
   return run_gemm(r);
 }
 

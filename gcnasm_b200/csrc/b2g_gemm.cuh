@@ -36,7 +36,12 @@
 namespace b2g {
 
 enum Mode : int { kModePlain = 0, kModeMX = 1, kModeBlk = 2 };
-enum OutMode : int { kOutStore = 0, kOutAtomic = 1, kOutWorkspace = 2 };
+// kOutPeers: column-parallel multi-GPU use -- every element (m, n) of this call's C is
+// stored into each peer buffer at peer_c[i] + m * peer_ldc + peer_col0 + n (the
+// caller's full-width C on every GPU of the job, mapped into this process), so
+// no all-gather follows the GEMM.
+enum OutMode : int { kOutStore = 0, kOutAtomic = 1, kOutWorkspace = 2, kOutPeers = 3 };
+constexpr int kMaxPeers = 8;
 
 struct GemmParams {
   // C as a (N, M, batch) TMA map with (64 bytes of columns) x 32 rows boxes; used
@@ -50,6 +55,9 @@ struct GemmParams {
   long long ldc, c_bstride;
   int out_mode;
   float* ws;  // split-K workspace [S][batch][M][N] fp32 (out_mode == kOutWorkspace)
+  void* peer_c[kMaxPeers];  // out_mode == kOutPeers
+  int n_peers, peer_first;  // peer_first: this GPU's index, where a tile's round of peer stores starts
+  long long peer_ldc, peer_col0;
   float alpha;
   // MX: UE8M0 scales in the tensor-core atom layout (128 rows x 4 K-blocks per
   // 512-byte atom, atoms [row_block][k_block]); *_rb = bytes between row blocks
@@ -75,6 +83,66 @@ struct GemmParams {
 struct Unit {
   int b, mt, nt, ks, kb0, kb1;
 };
+
+// Epilogue write to every peer: this warp's 32 rows (row0 + lane) x NC columns
+// (col0 + j, values acc[j] of the lane's row) of this call's C into each peer
+// buffer.  A lane holds one row, so its own stores would scatter 16-byte pieces
+// over 32 rows -- one small NVLink transaction each.  Instead 16 rows x 128 bytes
+// of columns at a time are staged in the warp's 2 KB of shared memory and read
+// back so that every warp-wide store writes four rows as whole 128-byte runs.
+// The peers are taken in a different order per tile and GPU so the GPUs' store
+// streams spread over the destinations.
+// (not inlined: its working set stays off the kernels' main epilogue path)
+template <int NC, bool kF32>
+__device__ __noinline__ void peer_store_warp(const GemmParams& p, const float (&acc)[NC], int row0, int col0,
+                                             int tile, uint8_t* stage, int lane) {
+  constexpr int CW = kF32 ? 32 : 64;  // columns in 128 bytes
+  constexpr int EP = kF32 ? 4 : 8;    // elements in 16 bytes
+  const int first = (p.peer_first + tile) % p.n_peers;
+  const int es = kF32 ? 4 : 2;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {         // rows row0 + 16h .. + 15
+#pragma unroll
+    for (int c = 0; c < NC / CW; ++c) {  // columns col0 + c*CW .. + CW - 1
+      __syncwarp();
+      if ((lane >> 4) == h) {
+        uint4* dst = reinterpret_cast<uint4*>(stage + (lane & 15) * 128);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          if (kF32)
+            dst[q] = make_uint4(__float_as_uint(acc[c * CW + 4 * q]), __float_as_uint(acc[c * CW + 4 * q + 1]),
+                                __float_as_uint(acc[c * CW + 4 * q + 2]), __float_as_uint(acc[c * CW + 4 * q + 3]));
+          else
+            dst[q] = make_uint4(pack_bf16x2(acc[c * CW + 8 * q], acc[c * CW + 8 * q + 1]),
+                                pack_bf16x2(acc[c * CW + 8 * q + 2], acc[c * CW + 8 * q + 3]),
+                                pack_bf16x2(acc[c * CW + 8 * q + 4], acc[c * CW + 8 * q + 5]),
+                                pack_bf16x2(acc[c * CW + 8 * q + 6], acc[c * CW + 8 * q + 7]));
+        }
+      }
+      __syncwarp();
+      // piece i*32 + lane of the staged 16 x 128 bytes: row (..)/8, 16-byte piece (..)%8;
+      // re-read from shared memory per peer so that only one piece is live at a time
+      for (int t = 0; t < p.n_peers; ++t) {
+        int q = first + t;
+        if (q >= p.n_peers) q -= p.n_peers;
+        uint8_t* base = static_cast<uint8_t*>(p.peer_c[q]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int idx = i * 32 + lane;
+          const int r = idx >> 3, pc = idx & 7;
+          const int m = row0 + 16 * h + r;
+          const int n = col0 + c * CW + pc * EP;
+          if (m < p.M && n < p.N) {
+            const uint4 v = reinterpret_cast<const uint4*>(stage + r * 128)[pc];
+            st_global_v4(base + (static_cast<long long>(m) * p.peer_ldc + p.peer_col0 + n) * es, v.x, v.y, v.z,
+                         v.w);
+          }
+        }
+      }
+    }
+  }
+  __syncwarp();
+}
 
 // Epilogue write through TMA: this warp's 32 rows (row0 + lane) x NC columns
 // (col0 + j, values acc[j] of the lane's row) of C, converted to the output type
@@ -447,6 +515,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       // ---- write the row segment [col0, col0 + NC) of row m
       if (p.tma_store && p.out_mode == kOutStore) {
         tma_store_rows<NC, Cfg::kOutF32>(&p.tm_c, acc, col0, w.mt * 128 + quad * 32, w.b, stage_c, lane);
+      } else if (kMode != kModeBlk && p.out_mode == kOutPeers) {  // the peer entry point is MX only
+        peer_store_warp<NC, Cfg::kOutF32>(p, acc, w.mt * 128 + quad * 32, col0, w.mt * p.NT + w.nt, stage_c, lane);
       } else if (m < p.M) {
         if (p.out_mode == kOutWorkspace) {
           float* dst = p.ws + ((static_cast<long long>(w.ks) * p.batch + w.b) * p.M + m) * static_cast<long long>(p.N);
@@ -479,6 +549,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       }
     }
     if (lane == 0) bulk_wait_all();  // this warp's TMA stores of C are complete
+    if (p.out_mode == kOutPeers) __threadfence_system();  // peer stores visible to every GPU
   }
 
   // ------------------------------------------------------------ teardown

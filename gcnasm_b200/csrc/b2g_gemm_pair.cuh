@@ -261,6 +261,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       for (int j = 0; j < NC; ++j) acc[j] = __uint_as_float(v[j]) * p.alpha;
       if (p.tma_store && p.out_mode == kOutStore) {
         tma_store_rows<NC, Cfg::kOutF32>(&p.tm_c, acc, col0, w.mt * 256 + static_cast<int>(rank) * 128 + quad * 32, w.b, stage_c, lane);
+      } else if (p.out_mode == kOutPeers) {
+        peer_store_warp<NC, Cfg::kOutF32>(p, acc, w.mt * 256 + static_cast<int>(rank) * 128 + quad * 32, col0,
+                                          w.mt * p.NT + w.nt, stage_c, lane);
       } else if (m < p.M) {
         if (p.out_mode == kOutWorkspace) {
           float* dst = p.ws + ((static_cast<long long>(w.ks) * p.batch + w.b) * p.M + m) * static_cast<long long>(p.N);
@@ -293,6 +296,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       }
     }
     if (lane == 0) bulk_wait_all();  // this warp's TMA stores of C are complete
+    if (p.out_mode == kOutPeers) __threadfence_system();  // peer stores visible to every GPU
   }
 
   // ------------------------------------------------------------ teardown

@@ -120,6 +120,24 @@ def mxfp8_gemm(a: torch.Tensor, b: torch.Tensor, sfa_tc: torch.Tensor, sfb_tc: t
     return out
 
 
+def mxfp8_gemm_peer_out(a: torch.Tensor, b: torch.Tensor, sfa_tc: torch.Tensor, sfb_tc: torch.Tensor,
+                        c_full: torch.Tensor, peer_ptrs, self_index: int, col_offset: int, alpha: float = 1.0,
+                        b_preshuffled: bool = False, stream=None) -> None:
+    """This GPU's columns [col_offset, col_offset + N) of C = alpha * A . B^T (B: [N, K],
+    this GPU's column slab) stored straight into every GPU's full-width C
+    (b2g_gemm_mxfp8_peer_out).  c_full is this GPU's [M, ldd] buffer (bf16 or fp32);
+    peer_ptrs[i] the base address of GPU i's buffer as mapped in this process."""
+    m, k = a.shape
+    n = b.shape[0]
+    args = capi.Mxfp8Args(a.data_ptr(), b.data_ptr(), sfa_tc.data_ptr(), sfb_tc.data_ptr(), 0,
+                          m, n, k, a.stride(0), k if b_preshuffled else b.stride(0), 0, alpha,
+                          int(b_preshuffled), _out_code(c_full.dtype), 0)
+    ptrs = (C.c_void_p * len(peer_ptrs))(*[C.c_void_p(int(x)) for x in peer_ptrs])
+    capi.check(capi.lib().b2g_gemm_mxfp8_peer_out(C.byref(args), ptrs, len(peer_ptrs), self_index,
+                                                  c_full.stride(0), col_offset, _stream(stream)),
+               "b2g_gemm_mxfp8_peer_out")
+
+
 def opus_kargs(a, b, c, sfa=None, sfb=None, stride_sfa=0, stride_sfb=0, batch=1,
                stride_sfa_batch=0, stride_sfb_batch=0) -> capi.OpusGemmKargs:
     """Fill opus_gemm_kargs the way the reference hosts do

@@ -6,6 +6,10 @@
 * N-shard (column parallel): rank g owns columns [col0, col0 + cols) of B / SFB
   / C and A is replicated; the bf16 column slabs are all-gathered over NCCL
   (NVLink) into [G, M, cols] and transposed locally into [M, N].
+* N-shard with the gather folded into the GEMM: every rank's full-width C lives
+  in symmetric memory (mapped into every process); each rank's GEMM epilogue
+  stores its columns straight into all ranks' C over NVLink, and a one-element
+  NCCL all-reduce on the stream orders the ranks before C is read.
 
 The local compute step is injectable so that the partition / gather logic can be
 exercised on CPU ranks (gloo) with a CPU stand-in; in production it is
@@ -61,3 +65,30 @@ def n_sharded_allgather(local_gemm: Callable[[int, int], torch.Tensor], N: int, 
     slabs = [torch.empty_like(c_local) for _ in range(world)]
     dist.all_gather(slabs, c_local, group=group)
     return torch.stack(slabs, 0).permute(1, 0, 2).reshape(c_local.shape[0], N)
+
+
+def peer_output(M: int, N: int, dtype: torch.dtype, group=None) -> tuple[torch.Tensor, list[int]]:
+    """This rank's full-width [M, N] C in torch symmetric memory and the base
+    address of every rank's C as mapped into this process (rank order)."""
+    from torch.distributed import _symmetric_memory as symm_mem
+
+    g = group if group is not None else dist.group.WORLD
+    c = symm_mem.empty((M, N), dtype=dtype, device=torch.device("cuda", torch.cuda.current_device()))
+    handle = symm_mem.rendezvous(c, g)
+    return c, [int(x) for x in handle.buffer_ptrs]
+
+
+def n_sharded_peer_out(qa: torch.Tensor, sfa: torch.Tensor, qb_local: torch.Tensor, sfb_local: torch.Tensor,
+                       c_full: torch.Tensor, peer_ptrs: list[int], N: int, world: int, rank: int,
+                       barrier: torch.Tensor, group=None) -> torch.Tensor:
+    """Column-parallel MXFP8 GEMM with the all-gather folded into its epilogue:
+    this rank's columns go straight into every rank's c_full; `barrier` (one
+    float32 element on this GPU) carries the all-reduce that orders the ranks
+    before any of them reads c_full.  Returns c_full, complete on every rank."""
+    from . import ops
+
+    col0, cols = col_range(N, world, rank)
+    assert qb_local.shape[0] == cols and len(peer_ptrs) == world
+    ops.mxfp8_gemm_peer_out(qa, qb_local, sfa, sfb_local, c_full, peer_ptrs, rank, col0)
+    dist.all_reduce(barrier, group=group)
+    return c_full

@@ -181,6 +181,21 @@ typedef struct b2g_mxfp8_args {
 
 B2G_API int b2g_gemm_mxfp8(const b2g_mxfp8_args* args, void* stream);
 
+/* Column-parallel MXFP8 GEMM for one GPU of a multi-GPU job with the output
+ * all-gather folded into the epilogue (no counterpart in the reference, whose
+ * GEMM hosts run on one GPU; it replaces "GEMM, then all-gather the bf16 column
+ * slabs"): C = alpha * A[M,K] . B[N,K]^T for this GPU's N columns is stored into
+ * every GPU's full-width C, element (m, n) at peer_d[i] + m * ldd_full +
+ * col_offset + n for i = 0 .. n_peers-1 (elements of out_dtype; args->d and
+ * args->ldd are not used, args->log2_k_split is ignored).  peer_d[self] is this
+ * GPU's own buffer, the others are the other GPUs' buffers mapped into this
+ * process (CUDA IPC or symmetric memory over NVLink); at most 8.  Row pitch and
+ * column offset must be whole 16 bytes.  Plain stores only: no kernel waits on
+ * another GPU, so the caller orders every GPU's call before reading C (a
+ * barrier on the stream, e.g. an NCCL all-reduce of one element). */
+B2G_API int b2g_gemm_mxfp8_peer_out(const b2g_mxfp8_args* args, void* const* peer_d, int n_peers, int self,
+                                    long long ldd_full, long long col_offset, void* stream);
+
 /* b2g_gemm_mxfp8 for callers that cannot allocate device memory.  No counterpart
  * in the reference (its host programs own every buffer and its kernels need no
  * scratch).  Some hosts hand all of the GPU's memory to their own pool at start-up

@@ -180,6 +180,26 @@ def test_invalid_arguments_return_status_without_gpu():
     assert b"K" in L.b2g_last_error() or len(L.b2g_last_error()) > 0
 
 
+def test_peer_out_validation_without_gpu():
+    """b2g_gemm_mxfp8_peer_out refuses bad peer lists, offsets and pitches before any
+    device work (fake, never dereferenced pointers)."""
+    L = capi.lib()
+    args = capi.Mxfp8Args(0x10000, 0x20000, 0x30000, 0x40000, 0, 512, 1024, 1024, 1024, 1024, 0, 1.0, 0,
+                          capi.OUT_BF16, 0)
+    ptrs = (C.c_void_p * 2)(0x100000, 0x200000)
+    assert L.b2g_gemm_mxfp8_peer_out(None, ptrs, 2, 0, 2048, 0, None) == capi.B2G_ERR_INVALID_ARG
+    assert L.b2g_gemm_mxfp8_peer_out(C.byref(args), ptrs, 0, 0, 2048, 0, None) == capi.B2G_ERR_INVALID_ARG
+    assert L.b2g_gemm_mxfp8_peer_out(C.byref(args), ptrs, 9, 0, 2048, 0, None) == capi.B2G_ERR_INVALID_ARG
+    assert L.b2g_gemm_mxfp8_peer_out(C.byref(args), ptrs, 2, 2, 2048, 0, None) == capi.B2G_ERR_INVALID_ARG
+    # columns [1536, 2560) do not fit 2048-column buffers
+    assert L.b2g_gemm_mxfp8_peer_out(C.byref(args), ptrs, 2, 1, 2048, 1536, None) == capi.B2G_ERR_INVALID_ARG
+    # bf16 column offset of 4 elements = 8 bytes
+    assert L.b2g_gemm_mxfp8_peer_out(C.byref(args), ptrs, 2, 1, 2048, 4, None) == capi.B2G_ERR_ALIGNMENT
+    bad = (C.c_void_p * 2)(0x100000, 0x200008)
+    assert L.b2g_gemm_mxfp8_peer_out(C.byref(args), bad, 2, 1, 2048, 1024, None) == capi.B2G_ERR_ALIGNMENT
+    assert b"peer" in L.b2g_last_error()
+
+
 def test_sf_tc_bytes():
     L = capi.lib()
     assert L.b2g_sf_tc_bytes(8192, 8192) == 64 * 64 * 512
