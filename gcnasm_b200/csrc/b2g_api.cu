@@ -1093,13 +1093,16 @@ int b2g_gemm_mxfp8_peer_out(const b2g_mxfp8_args* g, void* const* peer_d, int n_
 int b2g_gemm_mxfp8_f4gemm(const b2g_f4gemm_kargs* a, int bpreshuffle, int out_dtype, void* stream) {
   if (!a) return fail(B2G_ERR_INVALID_ARG, "null kargs");
   if (out_dtype != B2G_OUT_BF16 && out_dtype != B2G_OUT_F32) return fail(B2G_ERR_INVALID_ARG, "bad out_dtype");
-  if (a->beta != 0.0f) return fail(B2G_ERR_UNSUPPORTED, "beta != 0 (the C/bias path) is not supported");
   const int M = static_cast<int>(a->M), N = static_cast<int>(a->N), K = static_cast<int>(a->K);
   if (M <= 0 || N <= 0 || K <= 0) return fail(B2G_ERR_INVALID_ARG, "non-positive problem size");
   if (K % 32) return fail(B2G_ERR_UNSUPPORTED, "K %% 32 != 0");
   if (!a->ptr_ScaleA || !a->ptr_ScaleB || !a->ptr_A || !a->ptr_B || !a->ptr_D)
     return fail(B2G_ERR_INVALID_ARG, "null pointer in kargs");
   if (N % 16) return fail(B2G_ERR_UNSUPPORTED, "N (%d) must be a multiple of 16", N);
+  const bool with_c = a->beta != 0.0f && a->ptr_C;
+  if (with_c && ((static_cast<long long>(a->stride_C0) * (out_dtype == B2G_OUT_F32 ? 4 : 2)) % 16 ||
+                 !aligned16(a->ptr_C) || !aligned16(a->ptr_D)))
+    return fail(B2G_ERR_ALIGNMENT, "with beta, C and D need 16-byte aligned bases and row pitch");
   const int cols = K / 32;
   const int snA = static_cast<int>(a->stride_ScaleA0), snB = static_cast<int>(a->stride_ScaleB0);
   if (snA < cols || snA % 8 || snB < cols || snB % 8)
@@ -1119,6 +1122,14 @@ int b2g_gemm_mxfp8_f4gemm(const b2g_f4gemm_kargs* a, int bpreshuffle, int out_dt
   r.log2_k_split = a->log2_k_split;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   r.stream = st;
+  // D = alpha * A . B^T + beta * C (f4gemm_ref.hpp reference_gemm); beta is ignored
+  // without a C, as there.  With beta the GEMM writes alpha * A . B^T in fp32 to
+  // scratch and b2g_add_beta_c_kernel finishes D.
+  const bool out_f32 = r.out_f32;
+  if (with_c) {
+    r.out_f32 = true;
+    r.ldc = N;
+  }
   // One scratch block for the re-laid-out scales and the split-K workspace,
   // sized before anything is written into it (growing it later would free it).
   int bn = 0, S = 1, kb_per = 1;
@@ -1127,8 +1138,9 @@ int b2g_gemm_mxfp8_f4gemm(const b2g_f4gemm_kargs* a, int bpreshuffle, int out_dt
   const long long tcA = b2g_sf_tc_bytes(M, K), tcB = b2g_sf_tc_bytes(N, K);
   const size_t offB = static_cast<size_t>((tcA + 255) / 256 * 256);
   const size_t offW = offB + static_cast<size_t>((tcB + 255) / 256 * 256);
+  const size_t v_bytes = with_c ? (static_cast<size_t>(M) * N * 4 + 255) / 256 * 256 : 0;  // fp32 alpha * A . B^T
   void* ws = nullptr;
-  rc = workspace(d, offW + split_ws_bytes(r, S, d->sms), &ws);
+  rc = workspace(d, offW + v_bytes + split_ws_bytes(r, S, d->sms), &ws);
   if (rc) return rc;
   uint8_t* sA = static_cast<uint8_t*>(ws);
   uint8_t* sB = sA + offB;
@@ -1138,8 +1150,21 @@ int b2g_gemm_mxfp8_f4gemm(const b2g_f4gemm_kargs* a, int bpreshuffle, int out_dt
       static_cast<const uint8_t*>(a->ptr_ScaleB), N, cols, snB, sB);
   B2G_CUDA(cudaGetLastError());
   r.sfa = sA; r.sfb = sB;
-  r.ws_offset = offW;
-  return run_gemm(r);
+  r.ws_offset = offW + v_bytes;
+  if (!with_c) return run_gemm(r);
+  float* v = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + offW);
+  r.c = v;
+  rc = run_gemm(r);
+  if (rc) return rc;
+  const long long work = static_cast<long long>(M) * (N / 4);
+  if (out_f32)
+    b2g_add_beta_c_kernel<true><<<grid_for(work, 256, d->sms), 256, 0, st>>>(v, M, N, a->ptr_C, a->ptr_D,
+                                                                             a->stride_C0, a->beta);
+  else
+    b2g_add_beta_c_kernel<false><<<grid_for(work, 256, d->sms), 256, 0, st>>>(v, M, N, a->ptr_C, a->ptr_D,
+                                                                              a->stride_C0, a->beta);
+  B2G_CUDA(cudaGetLastError());
+  return maybe_sync_check();
 }
 
 int b2g_gemm_mxfp8_noalloc(const b2g_mxfp8_args* g, void* stream) {

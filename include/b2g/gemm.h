@@ -149,8 +149,8 @@ typedef struct B2G_PACKED b2g_f4gemm_kargs {
 #pragma pack(pop)
 #endif
 
-/* D[M, N] = alpha * A[M, K] . B[N, K]^T with MXFP8 operands (E4M3, one UE8M0
- * scale per 1x32 block of K).  Replaces Kernel::launch (asm_f4gemm/f4gemm.hpp:297-309)
+/* D[M, N] = alpha * A[M, K] . B[N, K]^T + beta * C[M, N] with MXFP8 operands (E4M3,
+ * one UE8M0 scale per 1x32 block of K).  Replaces Kernel::launch (asm_f4gemm/f4gemm.hpp:297-309)
  * over the kernarg block filled by fill_args (f4gemm.hpp:355-392):
  *   - ScaleA/ScaleB in the reference's padded + shuffled layout
  *     (asm_f4gemm/f4gemm_ref.hpp:101-130), stride_Scale*0 = padded columns;
@@ -158,7 +158,11 @@ typedef struct B2G_PACKED b2g_f4gemm_kargs {
  *   - log2_k_split > 0 splits K into 2^L parts (f4gemm.hpp:329-349); unlike the
  *     reference's bf16 atomics the partial sums are reduced in fp32, so the
  *     caller does NOT need to zero D first;
- *   - beta must be 0 (ptr_C unused), the only path the reference exercises.
+ *   - beta != 0 with ptr_C set adds beta * C as the reference CPU GEMM does
+ *     (f4gemm_ref.hpp:179-210: v = alpha * acc in fp32, v += beta * C, one rounding
+ *     to D's type); C has D's element type and D's row pitch stride_C0 (the
+ *     reference kernel reads stride_C0 for both) and may be D itself; without
+ *     ptr_C, beta is ignored, as there.
  * Contract: K % 32 == 0, N % 16 == 0. */
 B2G_API int b2g_gemm_mxfp8_f4gemm(const b2g_f4gemm_kargs* args, int bpreshuffle, int out_dtype, void* stream);
 

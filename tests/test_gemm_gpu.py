@@ -202,6 +202,36 @@ def test_f4gemm_abi_splitk(dev, oracle, split):
     check_out(dD, ref, torch.bfloat16)
 
 
+@pytest.mark.parametrize("out", ["bf16", "f32"])
+@pytest.mark.parametrize("split", [0, 2])
+@pytest.mark.parametrize("in_place", [False, True])
+def test_f4gemm_abi_beta(dev, oracle, out, split, in_place):
+    """D = alpha * A . B^T + beta * C through the f4gemm kernarg block
+    (f4gemm_ref.hpp:179-210: v = alpha * acc in fp32, then v += beta * C), C separate
+    from D or D itself; the reference formula is evaluated on the oracle's GEMM."""
+    from gcnasm_b200 import capi, f4gemm
+    M, N, K = 200, 512, 1024  # M not a multiple of the tile
+    od = torch.bfloat16 if out == "bf16" else torch.float32
+    sh = f4gemm.Shape(M, N, K)
+    qa, sa, qb, sb = mx_operands(oracle, M, N, K)
+    alpha, beta = 0.75, -1.25
+    acc = oracle.gemm_mx(qa, qb, sa, sb, M, N, K, acc_f64=True)
+    c_in = torch.from_numpy(oracle.normal_rows(99, 0, M, N)).to(od)
+    c_f = c_in.float().numpy().astype(np.float64)
+    ref = (np.float32(alpha) * acc.astype(np.float32)).astype(np.float64) + np.float64(np.float32(beta)) * c_f
+    dA = T(qa, dev)
+    dB = T(oracle.shuffle_weight_16x16(qb, N, K).reshape(N, K), dev)
+    dSA = T(oracle.shuffle_scale(sa, M, sh.Ks(), sh.scale_a_rows(), sh.scale_cols()), dev)
+    dSB = T(oracle.shuffle_scale(sb, N, sh.Ks(), sh.scale_b_rows(), sh.scale_cols()), dev)
+    dC = c_in.to(dev)
+    dD = dC if in_place else torch.full((M, N), float("nan"), dtype=od, device=dev)
+    args = f4gemm.fill_args(dD.data_ptr(), dC.data_ptr(), dA.data_ptr(), dB.data_ptr(), dSA.data_ptr(),
+                            dSB.data_ptr(), M, N, K, N, sh.scale_cols(), sh.scale_cols(), alpha, beta, split)
+    f4gemm.launch(args, 1, capi.OUT_F32 if out == "f32" else capi.OUT_BF16)
+    torch.cuda.synchronize()
+    check_out(dD, ref, od)
+
+
 # ------------------------------------------------------------------ opus block-scale paths
 @pytest.mark.parametrize("group_n", [128, 1])
 @pytest.mark.parametrize("M,N,K", [(256, 512, 256), (300, 512, 1024), (128, 1024, 2048)])

@@ -170,8 +170,8 @@ def test_invalid_arguments_return_status_without_gpu():
     assert L.b2g_gemm_a8w8_blockscale(C.byref(k), 128, 1, 0, None) == capi.B2G_ERR_ALIGNMENT
     k.ptr_a, k.m = 0x10000, 0
     assert L.b2g_gemm_a8w8_blockscale(C.byref(k), 128, 1, 0, None) == capi.B2G_ERR_INVALID_ARG
-    a = f4gemm.fill_args(0x1000, 0, 0x3000, 0x4000, 0x5000, 0x6000, 16, 4096, 4096, 4096, 128, 128, 1.0, 0.5, 0)
-    assert L.b2g_gemm_mxfp8_f4gemm(C.byref(a), 1, 0, None) == capi.B2G_ERR_UNSUPPORTED  # beta != 0
+    a = f4gemm.fill_args(0x1000, 0x2008, 0x3000, 0x4000, 0x5000, 0x6000, 16, 4096, 4096, 4096, 128, 128, 1.0, 0.5, 0)
+    assert L.b2g_gemm_mxfp8_f4gemm(C.byref(a), 1, 0, None) == capi.B2G_ERR_ALIGNMENT  # beta * C, C misaligned
     a = f4gemm.fill_args(0x1000, 0, 0x3000, 0x4000, 0x5000, 0x6000, 16, 4096, 4016, 4096, 128, 128, 1.0, 0.0, 0)
     assert L.b2g_gemm_mxfp8_f4gemm(C.byref(a), 1, 0, None) == capi.B2G_ERR_UNSUPPORTED  # K % 32
     assert L.b2g_shuffle_weight_16x16(None, None, 16, 32, None) == capi.B2G_ERR_INVALID_ARG
