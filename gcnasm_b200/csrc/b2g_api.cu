@@ -56,6 +56,7 @@ int fail(int code, const char* fmt, ...) {
   } while (0)
 
 std::atomic<unsigned long long> g_timeout_ns{4000ull * 1000000ull};
+std::atomic<int> g_static_weights{0};
 std::atomic<int> g_force_stall{0};
 
 // ------------------------------------------------------------------ driver entry
@@ -581,6 +582,7 @@ int run_skinny(const Req& r, const Env& d) {
   sp.status = d.status;
   sp.timeout_ns = g_timeout_ns.load();
   sp.debug_stall = g_force_stall.load();
+  sp.w_early = (g_static_weights.load() && use_pdl() && r.mode != kModeBlk) ? 1 : 0;
   sp.bsa = r.bsa;
   sp.bsb = r.bsb;
   sp.stride_sfa = r.stride_sfa;
@@ -934,6 +936,11 @@ const char* b2g_status_string(int s) {
 int b2g_set_wait_timeout_ms(int ms) {
   if (ms <= 0) return fail(B2G_ERR_INVALID_ARG, "timeout must be positive");
   g_timeout_ns.store(static_cast<unsigned long long>(ms) * 1000000ull);
+  return B2G_OK;
+}
+
+int b2g_set_static_weights(int on) {
+  g_static_weights.store(on ? 1 : 0);
   return B2G_OK;
 }
 

@@ -89,6 +89,7 @@ struct SkinnyParams {
   int* status;
   unsigned long long timeout_ns;
   int debug_stall;
+  int w_early;  // read B and its scales before the preceding kernel completes (static weights)
 };
 
 // CTA owning unit u when U units are split evenly over G CTAs (the largest c
@@ -173,26 +174,36 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
   // fill the stage's scale buffers completely).  B is read once: evict first,
   // so it does not push A, the scales and the partial slots out of L2.
   const uint64_t pol_w = l2_policy_evict_first();
-  auto issue = [&](long long u, int s) {
+  // the weights' part of a stage: arms the stage barrier with the whole stage's bytes
+  auto issue_w = [&](long long u, int s) {
     const int nt = static_cast<int>(u / p.KG);
     const int kb = static_cast<int>(u - static_cast<long long>(nt) * p.KG) * KBS;
     mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
     uint8_t* w_dst = smem + Cfg::kOffW + s * Cfg::kWBytes;
-    uint8_t* a_dst = smem + Cfg::kOffA + s * Cfg::kABytes;
     if (Cfg::kBPre)
       tma_load_4d_hint(w_dst, &tm_w, &full[s], 0, nt * 8, kb * 8, 0, pol_w);
     else if (p.kview)
       tma_load_3d_hint(w_dst, &tm_w, &full[s], 0, nt * 128, kb, pol_w);
     else
       tma_load_3d_hint(w_dst, &tm_w, &full[s], kb * 128, nt * 128, 0, pol_w);
+    if (kMode == kModeMX)
+      bulk_load(smem + Cfg::kOffSfw + s * Cfg::kSfBytes, p.sfw + nt * p.sf_rb + kb * 512, Cfg::kSfBytes, &full[s]);
+  };
+  // the activations' part
+  auto issue_a = [&](long long u, int s) {
+    const int nt = static_cast<int>(u / p.KG);
+    const int kb = static_cast<int>(u - static_cast<long long>(nt) * p.KG) * KBS;
+    uint8_t* a_dst = smem + Cfg::kOffA + s * Cfg::kABytes;
     if (p.kview)
       tma_load_3d(a_dst, &tm_a, &full[s], 0, 0, kb);
     else
       tma_load_3d(a_dst, &tm_a, &full[s], kb * 128, 0, 0);
-    if (kMode == kModeMX) {
-      bulk_load(smem + Cfg::kOffSfw + s * Cfg::kSfBytes, p.sfw + nt * p.sf_rb + kb * 512, Cfg::kSfBytes, &full[s]);
+    if (kMode == kModeMX)
       bulk_load(smem + Cfg::kOffSfa + s * Cfg::kSfBytes, p.sfa + kb * 512, Cfg::kSfBytes, &full[s]);
-    }
+  };
+  auto issue = [&](long long u, int s) {
+    issue_w(u, s);
+    issue_a(u, s);
   };
 
   // The producer thread initialises the barriers and fills the whole ring
@@ -207,8 +218,16 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     fence_mbar_init();
     tma_prefetch_desc(&tm_w);
     tma_prefetch_desc(&tm_a);
+    // Static weights (caller's promise: no kernel before this one on the stream
+    // writes B or its scales): their first ring fill streams while the preceding
+    // kernel finishes.
+    if (p.w_early)
+      for (int i = 0; i < pre; ++i) issue_w(u_lo + i, i);
     griddep_wait();  // launched as a programmatic dependent: the previous kernel's writes are visible after this
-    for (int i = 0; i < pre; ++i) issue(u_lo + i, i);
+    for (int i = 0; i < pre; ++i) {
+      if (!p.w_early) issue_w(u_lo + i, i);
+      issue_a(u_lo + i, i);
+    }
   }
   if (warp == 1) tmem_alloc<Cfg::kTmemCols>(tmem_holder);
   tc_fence_before();

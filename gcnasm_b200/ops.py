@@ -120,6 +120,12 @@ def mxfp8_gemm(a: torch.Tensor, b: torch.Tensor, sfa_tc: torch.Tensor, sfb_tc: t
     return out
 
 
+def set_static_weights(on: bool) -> None:
+    """b2g_set_static_weights: let decode GEMMs (M <= 128) read B and its scales
+    before the preceding kernel on the stream completes (weights no kernel writes)."""
+    capi.check(capi.lib().b2g_set_static_weights(int(bool(on))), "b2g_set_static_weights")
+
+
 def mxfp8_gemm_peer_out(a: torch.Tensor, b: torch.Tensor, sfa_tc: torch.Tensor, sfb_tc: torch.Tensor,
                         c_full: torch.Tensor, peer_ptrs, self_index: int, col_offset: int, alpha: float = 1.0,
                         b_preshuffled: bool = False, stream=None) -> None:

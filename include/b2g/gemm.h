@@ -258,6 +258,15 @@ B2G_API int b2g_quant_128x128(const float* x, int n, int k, void* q, float* sf, 
 B2G_API int b2g_device_status(int* status, int clear);
 /* Per-wait time limit of the kernels' barrier waits, in milliseconds (default 4000). */
 B2G_API int b2g_set_wait_timeout_ms(int ms);
+
+/* Static weights (no counterpart in the reference; a serving-loop setting).  When
+ * on, the decode GEMM (M <= 128, MX / plain FP8) may read B and its scales before
+ * the kernel preceding it on the stream has completed -- launched as a
+ * programmatic dependent, its first weight loads overlap that kernel's tail; A,
+ * A's scales and every write still wait for it.  Only for weights that no kernel
+ * earlier on the stream writes while it is on (e.g. the layers of a model being
+ * served).  Default off.  Process-wide; returns B2G_OK. */
+B2G_API int b2g_set_static_weights(int on);
 /* Test hook: while on, every GEMM launch makes its MMA issuer wait on a barrier
  * nothing arrives on, so the bounded wait runs out and the kernel reports
  * B2G_ERR_DEVICE_TIMEOUT through b2g_device_status. */

@@ -540,3 +540,44 @@ def test_blockscale_skinny(dev, oracle, M, N, K, group_n, out):
     again = ops.gemm_a8w8_blockscale(*args, group_n=group_n, out_dtype=od)
     torch.cuda.synchronize()
     assert torch.equal(first, again)
+
+
+def test_static_weights_decode_waits_for_activations(dev, oracle):
+    """With static weights on, a decode GEMM streams B before the preceding kernel
+    ends but must still read A after it: A is overwritten by an elementwise kernel
+    (not a memcpy, so the GEMM is launched as its programmatic dependent) right
+    before each GEMM on the same stream, eagerly and in a replayed CUDA graph, and
+    every result is the GEMM of the new A."""
+    from gcnasm_b200 import ops
+    M, N, K = 16, 4096, 4096
+    qa1, sa1, qb, sb = mx_operands(oracle, M, N, K)
+    qa2, _, _, _ = mx_operands(oracle, M, N, K, seed_a=4321)
+    sfb = T(oracle.sf_to_tc_layout(sb), dev)
+    sfa = T(oracle.sf_to_tc_layout(sa1), dev)  # kept for both: only the bytes of A change
+    b = T(qb, dev)
+    a_src = [T(qa1, dev), T(qa2, dev)]
+    want = [ops.mxfp8_gemm(x, b, sfa, sfb, out_dtype=torch.float32) for x in a_src]
+    assert not torch.equal(want[0], want[1])
+    a = torch.empty_like(a_src[0])
+    out = torch.empty((M, N), dtype=torch.float32, device=dev)
+    ops.set_static_weights(True)
+    try:
+        for i in range(6):
+            torch.bitwise_or(a_src[i % 2], 0, out=a)
+            ops.mxfp8_gemm(a, b, sfa, sfb, out=out)
+            torch.cuda.synchronize()
+            assert torch.equal(out, want[i % 2]), i
+        outs = [torch.empty_like(out) for _ in range(4)]
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(4):
+                torch.bitwise_or(a_src[i % 2], 0, out=a)
+                ops.mxfp8_gemm(a, b, sfa, sfb, out=outs[i])
+        for _ in range(2):
+            g.replay()
+            torch.cuda.synchronize()
+            for i in range(4):
+                assert torch.equal(outs[i], want[i % 2]), i
+    finally:
+        ops.set_static_weights(False)
+    assert ops.device_status() == 0
