@@ -575,7 +575,16 @@ int run_skinny(const Req& r, const Env& d) {
   sp.NT = cdiv(r.N, 128);
   sp.KG = cdiv(r.K, 128) / kkb;
   sp.kview = r.K % 128 == 0 ? 1 : 0;
-  sp.units = static_cast<long long>(sp.NT) * sp.KG;
+  const int grid = static_cast<int>(std::min<long long>(skinny_units(r), d.sms));
+  // Whole tiles per CTA, worked after the stream-K units so that every split
+  // tile's fix-up overlaps streaming; one less when the leftover tiles would
+  // give each CTA under half a tile of stream-K work (many pieces per tile).
+  // The blockwise kernel splits every tile stream-K.
+  int dp_w = r.mode == kModeBlk ? 0 : sp.NT / grid;
+  if (dp_w > 0 && 2 * (sp.NT - dp_w * grid) < grid) --dp_w;
+  sp.dp_w = dp_w;
+  sp.sk_tiles = sp.NT - dp_w * grid;
+  sp.units = static_cast<long long>(sp.sk_tiles) * sp.KG;
   sp.cnt = d.tile_cnt;
   // tags are nonzero and below 2^48 (the counter keeps 16 bits of arrivals)
   sp.tag = (g_skinny_tag.fetch_add(1) % ((1ull << 48) - 1)) + 1;
@@ -627,7 +636,6 @@ int run_skinny(const Req& r, const Env& d) {
   }
   if (rc) return rc;
 
-  const int grid = static_cast<int>(std::min<long long>(sp.units, d.sms));
   void* ws = nullptr;
   rc = env_workspace(d, r.ws_offset + split_ws_bytes(r, 1, d.sms), &ws);
   if (rc) return rc;

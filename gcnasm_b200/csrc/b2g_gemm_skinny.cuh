@@ -5,15 +5,19 @@
 // The product is computed transposed: the MMA's M = 128 runs over 128 rows of
 // B (weights) and its N = MP (M rounded up to 16/32/64/128) over the rows of A,
 // so no tensor-core rows are spent on padding.  Work units are (128-row B tile,
-// group of kKB 128-K blocks); they are split evenly over the persistent CTAs
-// (stream-K): CTA c takes units [c*U/G, (c+1)*U/G), which may begin or end
-// inside a tile.  Each contiguous run of one tile's units ("segment")
-// accumulates in TMEM.  A tile covered by a single segment is written straight
-// to C.  Otherwise every segment stores its fp32 partial to scratch and counts
-// itself in the tile's arrival counter; the last to arrive adds the partials
-// in segment order (a fixed order, so results do not depend on timing),
-// applies alpha and writes C in the output type.  One launch per call: no
-// zeroing pass, no atomics on C, no separate cast.
+// group of kKB 128-K blocks).  With NT tiles over G persistent CTAs, every CTA
+// owns W = NT / G whole tiles (one less when the remainder would be spread too
+// thin) and the units of the other NT - W*G tiles are split evenly over the
+// CTAs (stream-K): CTA c takes stream-K units [c*U/G, (c+1)*U/G), which may
+// begin or end inside a tile, and works through them before its whole tiles.
+// Each contiguous run of one tile's units ("segment") accumulates in TMEM.  A
+// tile covered by a single segment is written straight to C.  Otherwise every
+// segment stores its fp32 partial to scratch and counts itself in the tile's
+// arrival counter; the last to arrive adds the partials in segment order (a
+// fixed order, so results do not depend on timing), applies alpha and writes C
+// in the output type.  Because the split tiles come first, their fix-ups run
+// while the whole tiles stream, and every CTA ends on a plain TMEM -> C store.
+// One launch per call: no zeroing pass, no atomics on C, no separate cast.
 //
 // Decode GEMMs are bound by streaming B from HBM: every SM streams an equal
 // share of B through a deep ring (128-256 KB of B in flight per SM), and a
@@ -80,9 +84,11 @@ struct SkinnyParams {
   long long stride_sfa, stride_sfb;
   int group_n;
   int NT, KG;          // 128-row weight tiles; K groups (kKB blocks each) per tile
+  int sk_tiles;        // tiles [0, sk_tiles) are split stream-K; the rest are whole tiles
+  int dp_w;            // whole tiles per CTA: CTA c owns tiles sk_tiles + c*dp_w + [0, dp_w)
   int kview;           // 1: operand maps are (128, rows, K/128) views, coordinates (0, row, k_block);
                        // 0: (K, rows, 1) maps, coordinates (k_block * 128, row, 0)
-  long long units;     // NT * KG
+  long long units;     // stream-K units: sk_tiles * KG
   float* part;         // partial slots [2 * gridDim.x][kMP][128] fp32
   unsigned long long* cnt;  // per-tile arrival counters, (tag << 16) | arrivals
   unsigned long long tag;   // this launch's counter tag (nonzero, < 2^48)
@@ -167,7 +173,20 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
 
   const long long U = p.units;
   const int G = gridDim.x;
+  // This CTA's work, walked by position q in [0, nq): stream-K units [u_lo, u_hi),
+  // then the units [dp_lo, dp_lo + dp_w * KG) of its whole tiles.
   const long long u_lo = U * blockIdx.x / G, u_hi = U * (blockIdx.x + 1) / G;
+  const long long dp_lo = (static_cast<long long>(p.sk_tiles) + static_cast<long long>(blockIdx.x) * p.dp_w) * p.KG;
+  const long long nsk = u_hi - u_lo, nq = nsk + static_cast<long long>(p.dp_w) * p.KG;
+  auto unit_at = [&](long long q) { return q < nsk ? u_lo + q : dp_lo + (q - nsk); };
+  // units from position q to the end of its segment (a tile's run of units)
+  auto seg_len = [&](long long q) -> long long {
+    if (q < nsk) {
+      const long long tile_end = (u_lo + q) / p.KG * p.KG + p.KG;
+      return (u_hi < tile_end ? u_hi : tile_end) - (u_lo + q);
+    }
+    return p.KG - (q - nsk) % p.KG;
+  };
   const uint64_t tmo = p.timeout_ns;
 
   // One stage of loads: B tile(s), A rows and, for MX, both scale atoms (which
@@ -208,7 +227,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
 
   // The producer thread initialises the barriers and fills the whole ring
   // before the block-wide sync, so HBM traffic starts while TMEM is allocated.
-  const int pre = static_cast<int>(u_hi - u_lo < ST ? u_hi - u_lo : ST);
+  const int pre = static_cast<int>(nq < ST ? nq : ST);
   if (threadIdx.x == 0) {
     for (int s = 0; s < ST; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
     for (int s = 0; s < AS; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], 4); }
@@ -222,11 +241,11 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     // writes B or its scales): their first ring fill streams while the preceding
     // kernel finishes.
     if (p.w_early)
-      for (int i = 0; i < pre; ++i) issue_w(u_lo + i, i);
+      for (int i = 0; i < pre; ++i) issue_w(unit_at(i), i);
     griddep_wait();  // launched as a programmatic dependent: the previous kernel's writes are visible after this
     for (int i = 0; i < pre; ++i) {
-      if (!p.w_early) issue_w(u_lo + i, i);
-      issue_a(u_lo + i, i);
+      if (!p.w_early) issue_w(unit_at(i), i);
+      issue_a(unit_at(i), i);
     }
   }
   if (warp == 1) tmem_alloc<Cfg::kTmemCols>(tmem_holder);
@@ -243,9 +262,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       int s = pre % ST;
       uint32_t ph = pre == ST ? 1u : 0u;
       uint32_t issued_mask = pre == ST ? (1u << ST) - 1u : (1u << pre) - 1u, issued_phase = 0;
-      for (long long u = u_lo + pre; u < u_hi; ++u) {
+      for (long long q = pre; q < nq; ++q) {
         if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, kDevTimeoutProducer, tmo)) break;
-        issue(u, s);
+        issue(unit_at(q), s);
         issued_mask |= 1u << s;
         issued_phase = (issued_phase & ~(1u << s)) | (ph << s);
         if (++s == ST) { s = 0; ph ^= 1; }
@@ -266,15 +285,13 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       uint32_t ph = 0, aph = 0, sfbuf = 0;
       bool ok = true;
       if (p.debug_stall) ok = mbar_wait(never, 0, abort_flag, p.status, kDevTimeoutMma, tmo);
-      long long u = u_lo;
-      while (ok && u < u_hi) {
-        const int nt = static_cast<int>(u / p.KG);
-        const long long tile_end = static_cast<long long>(nt + 1) * p.KG;
-        const long long seg_end = u_hi < tile_end ? u_hi : tile_end;
+      long long q = 0;
+      while (ok && q < nq) {
+        const long long len = seg_len(q);
         if (!mbar_wait(&acc_empty[as], aph ^ 1, abort_flag, p.status, kDevTimeoutMma, tmo)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + as * Cfg::kAccStride;
-        for (long long v = u; v < seg_end; ++v) {
+        for (long long v = 0; v < len; ++v) {
           if (!mbar_wait(&full[s], ph, abort_flag, p.status, kDevTimeoutMma, tmo)) { ok = false; break; }
           tc_fence_after();
 #pragma unroll
@@ -294,7 +311,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
               const uint64_t wdesc = Cfg::kBPre ? desc_kmajor_interleave(w_base + kk * 2 * (128 * 16), 128 * 16)
                                                 : desc_kmajor_sw128(w_base + kk * 32);
               const uint64_t adesc = desc_kmajor_sw128(a_base + kk * 32);
-              const uint32_t acc = (v > u || j > 0 || kk > 0);
+              const uint32_t acc = (v > 0 || j > 0 || kk > 0);
               if (kMode == kModeMX)
                 mma_mxf8f6f4(d_tmem, wdesc, adesc, idesc_mxf8f6f4(128, MP, kk, kk), tmem_base + Cfg::kSfCol + sf_off,
                              tmem_base + Cfg::kSfCol + sf_off + 4, acc);
@@ -308,7 +325,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         if (!ok) break;
         tc_commit(&acc_full[as]);
         if (++as == AS) { as = 0; aph ^= 1; }
-        u = seg_end;
+        q += len;
       }
       tc_commit(fin);
       volatile int no_abort = 0;
@@ -334,15 +351,17 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     const int cta = static_cast<int>(blockIdx.x);
     int as = 0;
     uint32_t aph = 0;
-    long long u = u_lo;
-    while (u < u_hi) {
-      const int nt = static_cast<int>(u / p.KG);
+    long long q = 0;
+    while (q < nq) {
+      const long long len = seg_len(q);
+      const bool in_sk = q < nsk;
+      const int nt = static_cast<int>(unit_at(q) / p.KG);
       const long long t0 = static_cast<long long>(nt) * p.KG;
-      const long long seg_end = u_hi < t0 + p.KG ? u_hi : t0 + p.KG;
-      const int c0 = skinny_owner(t0, U, G), c1 = skinny_owner(t0 + p.KG - 1, U, G);
+      // pieces of a stream-K tile are owned by CTAs c0 .. c1; a whole tile is one piece
+      const int c0 = in_sk ? skinny_owner(t0, U, G) : cta, c1 = in_sk ? skinny_owner(t0 + p.KG - 1, U, G) : cta;
       const int nseg = c1 - c0 + 1;
       const int j = cta - c0;  // this piece's index in the tile
-      const bool fin_seg = seg_end == u_hi;
+      const bool fin_seg = in_sk && q + len == nsk;  // this CTA's last stream-K piece
       unsigned long long* cnt = p.cnt + nt;
       const unsigned long long all_others = (p.tag << 16) | static_cast<unsigned long long>(nseg - 1);
       auto piece = [&](int jj) {  // this thread's column of piece jj's slot
@@ -485,7 +504,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[as]);
       if (++as == AS) { as = 0; aph ^= 1; }
-      u = seg_end;
+      q += len;
     }
   }
 
