@@ -371,6 +371,12 @@ int launch_pair(const Env& d, const CUtensorMap& ta, const CUtensorMap& tb, cons
 int dispatch_pair(const Env& d, int mode, int bn, bool pre, bool f32, const CUtensorMap& ta, const CUtensorMap& tb,
                   const CUtensorMap& tsa, const CUtensorMap& tsb, const PairParams& pp, cudaStream_t st) {
   if (bn != 256) return fail(B2G_ERR_UNSUPPORTED, "no pair kernel of width %d", bn);
+  if (mode == kModeMX4) {
+    if (pre) return f32 ? launch_pair<PairCfg<kModeMX4, 256, true, true>>(d, ta, tb, tsa, tsb, pp, st)
+                        : launch_pair<PairCfg<kModeMX4, 256, true, false>>(d, ta, tb, tsa, tsb, pp, st);
+    return f32 ? launch_pair<PairCfg<kModeMX4, 256, false, true>>(d, ta, tb, tsa, tsb, pp, st)
+               : launch_pair<PairCfg<kModeMX4, 256, false, false>>(d, ta, tb, tsa, tsb, pp, st);
+  }
   if (mode == kModeMX) {
     if (pre) return f32 ? launch_pair<PairCfg<kModeMX, 256, true, true>>(d, ta, tb, tsa, tsb, pp, st)
                         : launch_pair<PairCfg<kModeMX, 256, true, false>>(d, ta, tb, tsa, tsb, pp, st);
@@ -430,6 +436,12 @@ int plan_tiles(const Req& r, int sms, int* bn_out, int* S_out, int* kb_per_out, 
   *S_out = S;
   *kb_per_out = kb_per;
   return B2G_OK;
+}
+
+// Bytes between 128-row blocks of a tensor-core scale-atom buffer: one 512-byte
+// atom per 128 elements of K (an MXFP4 request's K counts bytes, two elements each).
+long long sf_row_block_bytes(const Req& r) {
+  return static_cast<long long>(cdiv(r.K, 128)) * 512 * (r.mode == kModeMX4 ? 2 : 1);
 }
 
 // Few rows of A (decode): the transposed stream-K kernel.
@@ -571,7 +583,7 @@ int run_skinny(const Req& r, const Env& d) {
   sp.alpha = r.alpha;
   sp.sfw = r.sfb;
   sp.sfa = r.sfa;
-  sp.sf_rb = static_cast<long long>(cdiv(r.K, 128)) * 512;
+  sp.sf_rb = sf_row_block_bytes(r);
   sp.NT = cdiv(r.N, 128);
   sp.KG = cdiv(r.K, 128) / kkb;
   sp.kview = r.K % 128 == 0 ? 1 : 0;
@@ -669,6 +681,9 @@ int run_skinny(const Req& r, const Env& d) {
   else if (r.mode == kModeMX)
     rc = r.bpre ? dispatch_skinny_mp<kModeMX, true>(d, mp, kkb, tw, ta, sp, grid, r.stream)
                 : dispatch_skinny_mp<kModeMX, false>(d, mp, kkb, tw, ta, sp, grid, r.stream);
+  else if (r.mode == kModeMX4)
+    rc = r.bpre ? dispatch_skinny_mp<kModeMX4, true>(d, mp, kkb, tw, ta, sp, grid, r.stream)
+                : dispatch_skinny_mp<kModeMX4, false>(d, mp, kkb, tw, ta, sp, grid, r.stream);
   else
     rc = r.bpre ? dispatch_skinny_mp<kModePlain, true>(d, mp, kkb, tw, ta, sp, grid, r.stream)
                 : dispatch_skinny_mp<kModePlain, false>(d, mp, kkb, tw, ta, sp, grid, r.stream);
@@ -683,6 +698,9 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
   if (r.N % 16) return fail(B2G_ERR_UNSUPPORTED, "N (%d) must be a multiple of 16", r.N);
   if (r.K % 16) return fail(B2G_ERR_UNSUPPORTED, "K (%d) must be a multiple of 16", r.K);
   if (r.mode == kModeMX && r.K % 32) return fail(B2G_ERR_UNSUPPORTED, "MXFP8 needs K %% 32 == 0 (K=%d)", r.K);
+  // MXFP4 requests carry K and the strides in bytes (two E2M1 elements per byte)
+  if (r.mode == kModeMX4 && r.K % 128)
+    return fail(B2G_ERR_UNSUPPORTED, "MXFP4 needs K %% 256 == 0 (K=%d elements)", 2 * r.K);
   if (r.mode == kModeBlk && r.K % 128) return fail(B2G_ERR_UNSUPPORTED, "block-scale GEMM needs K %% 128 == 0 (K=%d)", r.K);
   if (!aligned16(r.a) || !aligned16(r.b) || !aligned16(r.c)) return fail(B2G_ERR_ALIGNMENT, "A/B/C must be 16-byte aligned");
   if (r.lda < r.K || r.lda % 16) return fail(B2G_ERR_ALIGNMENT, "A row stride %lld must be >= K and a multiple of 16", r.lda);
@@ -692,7 +710,7 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
   if (r.ldc < r.N || (r.ldc * esz) % 16) return fail(B2G_ERR_ALIGNMENT, "C row stride %lld must be >= N and 16-byte aligned", r.ldc);
   if (r.batch > 1 && (r.a_bstride % 16 || r.b_bstride % 16 || (r.c_bstride * esz) % 16))
     return fail(B2G_ERR_ALIGNMENT, "batch strides must be 16-byte multiples");
-  if (r.mode == kModeMX) {
+  if (mode_mx(r.mode)) {
     if (!r.sfa || !r.sfb) return fail(B2G_ERR_INVALID_ARG, "null scale pointer");
     if (!aligned16(r.sfa) || !aligned16(r.sfb) || r.sfa_bstride % 16 || r.sfb_bstride % 16)
       return fail(B2G_ERR_ALIGNMENT, "scale buffers must be 16-byte aligned");
@@ -732,7 +750,7 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
   p.c = r.c; p.ldc = r.ldc; p.c_bstride = r.c_bstride;
   p.alpha = r.alpha;
   p.sfa = r.sfa; p.sfb = r.sfb;
-  p.sfa_rb = static_cast<long long>(cdiv(r.K, 128)) * 512;
+  p.sfa_rb = sf_row_block_bytes(r);
   p.sfb_rb = p.sfa_rb;
   p.sfa_bstride = r.sfa_bstride; p.sfb_bstride = r.sfb_bstride;
   p.sfb_blocks = cdiv(r.N, 128);
@@ -825,15 +843,16 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
     CUtensorMap tsa, tsb;
     memset(&tsa, 0, sizeof(tsa));
     memset(&tsb, 0, sizeof(tsb));
-    if (r.mode == kModeMX) {
-      const long long kb4 = cdiv(r.K, 128);
+    if (mode_mx(r.mode)) {
+      const int ka = mode_atoms(r.mode);  // K-atoms per 128-byte K block
+      const long long kb4 = cdiv(r.K, 128) * ka;
       for (int which = 0; which < 2; ++which) {
         const int rows = which ? r.N : r.M;
         const long long rb = cdiv(rows, 128);
         const long long bstr = which ? r.sfb_bstride : r.sfa_bstride;
         cuuint64_t dims[4] = {128, (cuuint64_t)kb4, (cuuint64_t)rb, (cuuint64_t)r.batch};
         cuuint64_t str[3] = {512, (cuuint64_t)(kb4 * 512), (cuuint64_t)(r.batch > 1 ? bstr : rb * kb4 * 512)};
-        cuuint32_t box[4] = {128, 1, (cuuint32_t)(which ? 2 : 1), 1};
+        cuuint32_t box[4] = {128, (cuuint32_t)ka, (cuuint32_t)(which ? 2 : 1), 1};
         rc = encode(which ? &tsb : &tsa, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, which ? (const void*)r.sfb : (const void*)r.sfa,
                     dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
         if (rc) return rc;
@@ -849,6 +868,7 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
   switch (r.mode) {
     case kModePlain: rc = dispatch_bn<kModePlain>(d, bn, r.bpre, r.out_f32, ta, tb, p, grid, r.stream); break;
     case kModeMX: rc = dispatch_bn<kModeMX>(d, bn, r.bpre, r.out_f32, ta, tb, p, grid, r.stream); break;
+    case kModeMX4: rc = dispatch_bn<kModeMX4>(d, bn, r.bpre, r.out_f32, ta, tb, p, grid, r.stream); break;
     default: rc = dispatch_bn<kModeBlk>(d, bn, r.bpre, r.out_f32, ta, tb, p, grid, r.stream); break;
   }
   if (rc) return rc;
@@ -1051,16 +1071,21 @@ long long b2g_sf_tc_bytes(int rows, int k) {
   return static_cast<long long>((rows + 127) / 128) * ((k / 32 + 3) / 4) * 512;
 }
 
-int b2g_gemm_mxfp8(const b2g_mxfp8_args* g, void* stream) {
+// b2g_gemm_mxfp8 / b2g_gemm_mxfp4: K and the A/B strides arrive in elements; an
+// MXFP4 request carries them in bytes (two E2M1 elements per byte).
+static int run_mx_native(const b2g_mxfp8_args* g, int mode, void* stream) {
   if (!g) return fail(B2G_ERR_INVALID_ARG, "null args");
   if (g->out_dtype != B2G_OUT_BF16 && g->out_dtype != B2G_OUT_F32) return fail(B2G_ERR_INVALID_ARG, "bad out_dtype");
+  const int per = mode == kModeMX4 ? 2 : 1;
+  if (per == 2 && (g->k % 2 || g->lda % 2 || (!g->b_preshuffled && g->ldb % 2)))
+    return fail(B2G_ERR_ALIGNMENT, "MXFP4 K and row strides count E2M1 elements and must be even");
   Req r;
-  r.mode = kModeMX;
+  r.mode = mode;
   r.bpre = g->b_preshuffled != 0;
   r.out_f32 = g->out_dtype == B2G_OUT_F32;
-  r.M = g->m; r.N = g->n; r.K = g->k;
-  r.a = g->a; r.lda = g->lda;
-  r.b = g->b; r.ldb = r.bpre ? g->k : g->ldb;
+  r.M = g->m; r.N = g->n; r.K = g->k / per;
+  r.a = g->a; r.lda = g->lda / per;
+  r.b = g->b; r.ldb = r.bpre ? g->k / per : g->ldb / per;
   r.c = g->d; r.ldc = g->ldd;
   r.alpha = g->alpha;
   r.sfa = static_cast<const uint8_t*>(g->sfa);
@@ -1069,6 +1094,10 @@ int b2g_gemm_mxfp8(const b2g_mxfp8_args* g, void* stream) {
   r.stream = static_cast<cudaStream_t>(stream);
   return run_gemm(r);
 }
+
+int b2g_gemm_mxfp8(const b2g_mxfp8_args* g, void* stream) { return run_mx_native(g, kModeMX, stream); }
+
+int b2g_gemm_mxfp4(const b2g_mxfp8_args* g, void* stream) { return run_mx_native(g, kModeMX4, stream); }
 
 int b2g_gemm_mxfp8_peer_out(const b2g_mxfp8_args* g, void* const* peer_d, int n_peers, int self,
                             long long ldd_full, long long col_offset, void* stream) {
@@ -1105,12 +1134,19 @@ int b2g_gemm_mxfp8_peer_out(const b2g_mxfp8_args* g, void* const* peer_d, int n_
   return run_gemm(r);
 }
 
-int b2g_gemm_mxfp8_f4gemm(const b2g_f4gemm_kargs* a, int bpreshuffle, int out_dtype, void* stream) {
+// The f4gemm kernarg entries.  Strides count elements (f4gemm.hpp:351-353: an
+// MXFP4 row of K elements is K/2 bytes); MXFP4 keeps the reference's K % 256 rule
+// (asm_f4gemm/main.cpp:141-150).
+static int run_mx_f4gemm(const b2g_f4gemm_kargs* a, int bpreshuffle, int out_dtype, void* stream, int mode) {
   if (!a) return fail(B2G_ERR_INVALID_ARG, "null kargs");
   if (out_dtype != B2G_OUT_BF16 && out_dtype != B2G_OUT_F32) return fail(B2G_ERR_INVALID_ARG, "bad out_dtype");
   const int M = static_cast<int>(a->M), N = static_cast<int>(a->N), K = static_cast<int>(a->K);
+  const int per = mode == kModeMX4 ? 2 : 1;  // elements per byte
   if (M <= 0 || N <= 0 || K <= 0) return fail(B2G_ERR_INVALID_ARG, "non-positive problem size");
   if (K % 32) return fail(B2G_ERR_UNSUPPORTED, "K %% 32 != 0");
+  if (per == 2 && K % 256) return fail(B2G_ERR_UNSUPPORTED, "MXFP4 needs K %% 256 == 0 (K=%d)", K);
+  if (per == 2 && (a->stride_A0 % 2 || (!bpreshuffle && a->stride_B0 % 2)))
+    return fail(B2G_ERR_ALIGNMENT, "MXFP4 A/B strides count E2M1 elements and must be even");
   if (!a->ptr_ScaleA || !a->ptr_ScaleB || !a->ptr_A || !a->ptr_B || !a->ptr_D)
     return fail(B2G_ERR_INVALID_ARG, "null pointer in kargs");
   if (N % 16) return fail(B2G_ERR_UNSUPPORTED, "N (%d) must be a multiple of 16", N);
@@ -1126,12 +1162,12 @@ int b2g_gemm_mxfp8_f4gemm(const b2g_f4gemm_kargs* a, int bpreshuffle, int out_dt
   int rc = device_state(&d);
   if (rc) return rc;
   Req r;
-  r.mode = kModeMX;
+  r.mode = mode;
   r.bpre = bpreshuffle != 0;
   r.out_f32 = out_dtype == B2G_OUT_F32;
-  r.M = M; r.N = N; r.K = K;
-  r.a = a->ptr_A; r.lda = a->stride_A0;
-  r.b = a->ptr_B; r.ldb = r.bpre ? K : static_cast<long long>(a->stride_B0);
+  r.M = M; r.N = N; r.K = K / per;
+  r.a = a->ptr_A; r.lda = a->stride_A0 / per;
+  r.b = a->ptr_B; r.ldb = r.bpre ? K / per : static_cast<long long>(a->stride_B0) / per;
   r.c = a->ptr_D; r.ldc = a->stride_C0;  // the reference kernels use stride_C0 for D
   r.alpha = a->alpha;
   r.log2_k_split = a->log2_k_split;
@@ -1180,6 +1216,14 @@ int b2g_gemm_mxfp8_f4gemm(const b2g_f4gemm_kargs* a, int bpreshuffle, int out_dt
                                                                               a->stride_C0, a->beta);
   B2G_CUDA(cudaGetLastError());
   return maybe_sync_check();
+}
+
+int b2g_gemm_mxfp8_f4gemm(const b2g_f4gemm_kargs* a, int bpreshuffle, int out_dtype, void* stream) {
+  return run_mx_f4gemm(a, bpreshuffle, out_dtype, stream, kModeMX);
+}
+
+int b2g_gemm_mxfp4_f4gemm(const b2g_f4gemm_kargs* a, int bpreshuffle, int out_dtype, void* stream) {
+  return run_mx_f4gemm(a, bpreshuffle, out_dtype, stream, kModeMX4);
 }
 
 int b2g_gemm_mxfp8_noalloc(const b2g_mxfp8_args* g, void* stream) {

@@ -7,6 +7,10 @@
 //                per-tensor alpha in the epilogue;
 //   kModeMX    : MXFP8, E4M3 with one UE8M0 scale per 1x32 K-block, applied by
 //                the tensor core (tcgen05.mma kind::mxf8f6f4.block_scale);
+//   kModeMX4   : MXFP4, packed E2M1 (two per byte, the asm_f4gemm operand format)
+//                with one UE8M0 scale per 1x32 K-block (kind::mxf4.block_scale);
+//                the host passes K and the row strides in bytes, so the tiles,
+//                maps and K loop are those of the FP8 modes;
 //   kModeBlk   : fp32 block scales, one per 1x128 of A and per 128x128 (GROUP_N=128,
 //                opus_gemm/block_scale_gemm) or 1x128 of B (GROUP_N=1,
 //                opus_gemm/block_scale_1x128x1_gemm).  Each 128-K block's MMA
@@ -35,7 +39,13 @@
 
 namespace b2g {
 
-enum Mode : int { kModePlain = 0, kModeMX = 1, kModeBlk = 2 };
+enum Mode : int { kModePlain = 0, kModeMX = 1, kModeBlk = 2, kModeMX4 = 3 };
+
+// The MX modes carry UE8M0 scale atoms (128 rows x 4 scales: 128 elements of K).
+// Operands are walked in 128-byte K blocks: 128 E4M3 elements (kModeMX, one atom
+// per block) or 256 packed E2M1 elements (kModeMX4, two atoms per block).
+__host__ __device__ constexpr bool mode_mx(int m) { return m == kModeMX || m == kModeMX4; }
+__host__ __device__ constexpr int mode_atoms(int m) { return m == kModeMX4 ? 2 : (m == kModeMX ? 1 : 0); }
 // kOutPeers: column-parallel multi-GPU use -- every element (m, n) of this call's C is
 // stored into each peer buffer at peer_c[i] + m * peer_ldc + peer_col0 + n (the
 // caller's full-width C on every GPU of the job, mapped into this process), so
@@ -216,22 +226,26 @@ struct GemmCfg {
 
   static constexpr int kABytes = kBM * kBK;
   static constexpr int kBBytes = kBN * kBK;
-  static constexpr int kSfaBytes = kMode == kModeMX ? 512 : 0;
+  static constexpr int kKAtoms = mode_atoms(kMode);  // scale atoms per 128-row block per stage
+  static constexpr int kSfaBytes = 512 * kKAtoms;
   static constexpr int kSfbAtoms = (kBN + 127) / 128;
-  static constexpr int kSfbBytes = kMode == kModeMX ? 512 * kSfbAtoms : 0;
+  static constexpr int kSfbBytes = 512 * kSfbAtoms * kKAtoms;
   static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
   static constexpr int kStages = (kBN == 256) ? 4 : 6;
 
   // TMEM: accumulator (or per-K-block partial) buffers, then the MX scales in two
   // alternating column sets (the copies for block k+1 never overwrite columns the
   // MMAs of block k still read)
-  static constexpr int kSfCols = kMode == kModeMX ? 4 + 4 * kSfbAtoms : 0;
+  static constexpr int kSfCols = 4 * kKAtoms * (1 + kSfbAtoms);
   static constexpr int kSfBufs = 2;
   // blockwise: as many per-K-block partial buffers as TMEM holds, so the MMAs run
   // up to three K blocks ahead of the promotion
   static constexpr int kAccStages = (kMode == kModeBlk) ? 512 / kBN : ((2 * kBN + kSfBufs * kSfCols <= 512) ? 2 : 1);
+  // per column set: A atoms (4 columns each, K-atom q at + 4q), then B atoms
+  // (K-atom q of row block j at + 4 * (q * kSfbAtoms + j): one K-atom's B scales
+  // are contiguous over the tile's rows, as the MMA reads them)
   static constexpr int kSfaCol = kAccStages * kBN;  // + buffer * kSfCols
-  static constexpr int kSfbCol = kSfaCol + 4;
+  static constexpr int kSfbCol = kSfaCol + 4 * kKAtoms;
   static constexpr int kTmemCols = 512;
 
   // shared memory carve-up (offsets from a 1024-byte aligned base)
@@ -275,7 +289,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  if (kMode == kModeMX) {  // scale atoms never fetched (tile edge) must hold a finite scale
+  if (mode_mx(kMode)) {  // scale atoms never fetched (tile edge) must hold a finite scale
     for (int i = threadIdx.x; i < ST * (Cfg::kSfaBytes + Cfg::kSfbBytes) / 4; i += Cfg::kThreads)
       reinterpret_cast<uint32_t*>(smem + Cfg::kOffSfa)[i] = 0x7F7F7F7Fu;
     fence_proxy_async_smem();
@@ -310,10 +324,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
           if (!mbar_wait(&empty[s], ph ^ 1, abort_flag, p.status, kDevTimeoutProducer, tmo)) { ok = false; break; }
           uint32_t tx = Cfg::kABytes + Cfg::kBBytes;
           int nsfb = 0;
-          if (kMode == kModeMX) {
+          if (mode_mx(kMode)) {
             nsfb = p.sfb_blocks - w.nt * Cfg::kSfbAtoms;
             nsfb = nsfb < Cfg::kSfbAtoms ? nsfb : Cfg::kSfbAtoms;
-            tx += 512u * (1 + nsfb);
+            tx += 512u * Cfg::kKAtoms * (1 + nsfb);
           }
           mbar_arrive_expect_tx(&full[s], tx);
           tma_load_3d(smem + Cfg::kOffA + s * Cfg::kABytes, &tm_a, &full[s], kb * 128, w.mt * 128, w.b);
@@ -321,12 +335,13 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             tma_load_4d(smem + Cfg::kOffB + s * Cfg::kBBytes, &tm_b, &full[s], 0, w.nt * (kBN / 16), kb * 8, w.b);
           else
             tma_load_3d(smem + Cfg::kOffB + s * Cfg::kBBytes, &tm_b, &full[s], kb * 128, w.nt * kBN, w.b);
-          if (kMode == kModeMX) {
+          if (mode_mx(kMode)) {  // the block's K-atoms of each 128-row block are contiguous
+            constexpr uint32_t kAB = 512u * Cfg::kKAtoms;
             bulk_load(smem + Cfg::kOffSfa + s * Cfg::kSfaBytes,
-                      p.sfa + w.b * p.sfa_bstride + w.mt * p.sfa_rb + kb * 512, 512, &full[s]);
+                      p.sfa + w.b * p.sfa_bstride + w.mt * p.sfa_rb + kb * kAB, kAB, &full[s]);
             for (int j = 0; j < nsfb; ++j)
-              bulk_load(smem + Cfg::kOffSfb + s * Cfg::kSfbBytes + j * 512,
-                        p.sfb + w.b * p.sfb_bstride + (w.nt * Cfg::kSfbAtoms + j) * p.sfb_rb + kb * 512, 512,
+              bulk_load(smem + Cfg::kOffSfb + s * Cfg::kSfbBytes + j * kAB,
+                        p.sfb + w.b * p.sfb_bstride + (w.nt * Cfg::kSfbAtoms + j) * p.sfb_rb + kb * kAB, kAB,
                         &full[s]);
           }
           issued_mask |= 1u << s;
@@ -367,13 +382,17 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
           const uint32_t d_tmem = tmem_base + as * kBN;
           const uint32_t sf_off = sfbuf * Cfg::kSfCols;
           sfbuf ^= 1;
-          if (kMode == kModeMX) {
-            tc_cp_32x128b_warpx4(tmem_base + Cfg::kSfaCol + sf_off,
-                                 desc_sf_atom(smem_u32(smem + Cfg::kOffSfa + s * Cfg::kSfaBytes)));
+          if (mode_mx(kMode)) {
 #pragma unroll
-            for (int j = 0; j < Cfg::kSfbAtoms; ++j)
-              tc_cp_32x128b_warpx4(tmem_base + Cfg::kSfbCol + sf_off + 4 * j,
-                                   desc_sf_atom(smem_u32(smem + Cfg::kOffSfb + s * Cfg::kSfbBytes + j * 512)));
+            for (int q = 0; q < Cfg::kKAtoms; ++q) {
+              tc_cp_32x128b_warpx4(tmem_base + Cfg::kSfaCol + sf_off + 4 * q,
+                                   desc_sf_atom(smem_u32(smem + Cfg::kOffSfa + s * Cfg::kSfaBytes + q * 512)));
+#pragma unroll
+              for (int j = 0; j < Cfg::kSfbAtoms; ++j)
+                tc_cp_32x128b_warpx4(tmem_base + Cfg::kSfbCol + sf_off + 4 * (q * Cfg::kSfbAtoms + j),
+                                     desc_sf_atom(smem_u32(smem + Cfg::kOffSfb + s * Cfg::kSfbBytes +
+                                                           (j * Cfg::kKAtoms + q) * 512)));
+            }
           }
 #pragma unroll
           for (int kk = 0; kk < Cfg::kBK / Cfg::kUmmaK; ++kk) {
@@ -384,6 +403,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             if (kMode == kModeMX)
               mma_mxf8f6f4(d_tmem, adesc, bdesc, idesc_mxf8f6f4(128, kBN, kk, kk), tmem_base + Cfg::kSfaCol + sf_off,
                            tmem_base + Cfg::kSfbCol + sf_off, acc);
+            else if (kMode == kModeMX4)  // K-atom kk / 2, byte pair 2 * (kk % 2)
+              mma_mxf4(d_tmem, adesc, bdesc, idesc_mxf4(128, kBN, (kk & 1) * 2, (kk & 1) * 2),
+                       tmem_base + Cfg::kSfaCol + sf_off + 4 * (kk >> 1),
+                       tmem_base + Cfg::kSfbCol + sf_off + 4 * Cfg::kSfbAtoms * (kk >> 1), acc);
             else
               mma_f8f6f4(d_tmem, adesc, bdesc, idesc_f8f6f4(128, kBN), acc);
           }

@@ -46,19 +46,22 @@ struct PairCfg {
   // scales span 2 atoms and the MMA's scale address is shifted by 0 or 2 TMEM
   // columns (the even shift CUTLASS's N=192 tiles use).
   static constexpr int kSfbAtoms = 2;
-  static constexpr int kSfaBytes = kMode == kModeMX ? 512 : 0;
-  static constexpr int kSfbBytes = kMode == kModeMX ? 512 * kSfbAtoms : 0;
+  static constexpr int kKAtoms = mode_atoms(kMode);  // scale K-atoms per 128-byte K block
+  static constexpr int kSfaBytes = 512 * kKAtoms;
+  static constexpr int kSfbBytes = 512 * kSfbAtoms * kKAtoms;
   static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
-  static constexpr int kStages = 6;
+  static constexpr int kStages = kMode == kModeMX4 ? 5 : 6;  // MXFP4's larger scale stages leave room for 5
   static constexpr uint32_t kTxPerStage = 2u * kStageBytes;  // both CTAs complete on the leader's barrier
 
   // Scale factors live in TMEM in two alternating column sets: the copies for
   // 128-K block k+1 then never overwrite columns the MMAs of block k still read.
-  static constexpr int kSfCols = kMode == kModeMX ? 4 + 4 * kSfbAtoms : 0;
+  // Per column set: A K-atom q at + 4q, then B K-atom q of row block j at
+  // + 4 * (q * kSfbAtoms + j).
+  static constexpr int kSfCols = 4 * kKAtoms * (1 + kSfbAtoms);
   static constexpr int kSfBufs = 2;
   static constexpr int kAccStages = (2 * kBN + kSfBufs * kSfCols <= 512) ? 2 : 1;
   static constexpr int kSfaCol = kAccStages * kBN;  // + buffer * kSfCols
-  static constexpr int kSfbCol = kSfaCol + 4;
+  static constexpr int kSfbCol = kSfaCol + 4 * kKAtoms;
   static constexpr int kTmemCols = 512;
 
   static constexpr int kOffA = 0;
@@ -132,7 +135,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tm_a);
       tma_prefetch_desc(&tm_b);
-      if (kMode == kModeMX) { tma_prefetch_desc(&tm_sfa); tma_prefetch_desc(&tm_sfb); }
+      if (mode_mx(kMode)) { tma_prefetch_desc(&tm_sfa); tma_prefetch_desc(&tm_sfb); }
       int s = 0;
       uint32_t ph = 0;
       uint32_t issued_mask = 0, issued_phase = 0;
@@ -150,10 +153,12 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             tma_load_4d_pair(smem + Cfg::kOffB + s * Cfg::kBBytes, &tm_b, bar, 0, brow / 16, kb * 8, w.b);
           else
             tma_load_3d_pair(smem + Cfg::kOffB + s * Cfg::kBBytes, &tm_b, bar, kb * 128, brow, w.b);
-          if (kMode == kModeMX) {
-            // scale atoms: (128 words, k-block, row block) boxes of the atom-layout buffers
-            tma_load_4d_pair(smem + Cfg::kOffSfa + s * Cfg::kSfaBytes, &tm_sfa, bar, 0, kb, w.mt * 2 + rank, w.b);
-            tma_load_4d_pair(smem + Cfg::kOffSfb + s * Cfg::kSfbBytes, &tm_sfb, bar, 0, kb, (w.nt * kBN) >> 7, w.b);
+          if (mode_mx(kMode)) {
+            // scale atoms: (128 words, K-atoms, row blocks) boxes of the atom-layout buffers,
+            // landing as [row block][K-atom][512 B]
+            const int ka = kb * Cfg::kKAtoms;
+            tma_load_4d_pair(smem + Cfg::kOffSfa + s * Cfg::kSfaBytes, &tm_sfa, bar, 0, ka, w.mt * 2 + rank, w.b);
+            tma_load_4d_pair(smem + Cfg::kOffSfb + s * Cfg::kSfbBytes, &tm_sfb, bar, 0, ka, (w.nt * kBN) >> 7, w.b);
           }
           issued_mask |= 1u << s;
           issued_phase = (issued_phase & ~(1u << s)) | (ph << s);
@@ -193,13 +198,17 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
           const uint32_t b_base = smem_u32(smem + Cfg::kOffB + s * Cfg::kBBytes);
           const uint32_t d_tmem = tmem_base + as * kBN;
           const uint32_t sf_off = sfbuf * Cfg::kSfCols;
-          if (kMode == kModeMX) {
-            tc_cp_32x128b_warpx4_pair(tmem_base + Cfg::kSfaCol + sf_off,
-                                      desc_sf_atom(smem_u32(smem + Cfg::kOffSfa + s * Cfg::kSfaBytes)));
+          if (mode_mx(kMode)) {
 #pragma unroll
-            for (int j = 0; j < Cfg::kSfbAtoms; ++j)
-              tc_cp_32x128b_warpx4_pair(tmem_base + Cfg::kSfbCol + sf_off + 4 * j,
-                                        desc_sf_atom(smem_u32(smem + Cfg::kOffSfb + s * Cfg::kSfbBytes + j * 512)));
+            for (int q = 0; q < Cfg::kKAtoms; ++q) {
+              tc_cp_32x128b_warpx4_pair(tmem_base + Cfg::kSfaCol + sf_off + 4 * q,
+                                        desc_sf_atom(smem_u32(smem + Cfg::kOffSfa + s * Cfg::kSfaBytes + q * 512)));
+#pragma unroll
+              for (int j = 0; j < Cfg::kSfbAtoms; ++j)
+                tc_cp_32x128b_warpx4_pair(tmem_base + Cfg::kSfbCol + sf_off + 4 * (q * Cfg::kSfbAtoms + j),
+                                          desc_sf_atom(smem_u32(smem + Cfg::kOffSfb + s * Cfg::kSfbBytes +
+                                                                (j * Cfg::kKAtoms + q) * 512)));
+            }
           }
           // B scales of tile row 0 sit ((nt * BN) % 128) / 32 TMEM columns into the first atom
           const uint32_t sfa_tmem = tmem_base + Cfg::kSfaCol + sf_off;
@@ -213,6 +222,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             const uint32_t acc = (kb > w.kb0 || kk > 0);
             if (kMode == kModeMX)
               mma_mxf8f6f4_pair(d_tmem, adesc, bdesc, idesc_mxf8f6f4(256, kBN, kk, kk), sfa_tmem, sfb_tmem, acc);
+            else if (kMode == kModeMX4)  // K-atom kk / 2, byte pair 2 * (kk % 2)
+              mma_mxf4_pair(d_tmem, adesc, bdesc, idesc_mxf4(256, kBN, (kk & 1) * 2, (kk & 1) * 2),
+                            sfa_tmem + 4 * (kk >> 1), sfb_tmem + 4 * Cfg::kSfbAtoms * (kk >> 1), acc);
             else
               mma_f8f6f4_pair(d_tmem, adesc, bdesc, idesc_f8f6f4(256, kBN), acc);
           }

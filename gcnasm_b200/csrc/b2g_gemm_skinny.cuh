@@ -22,8 +22,9 @@
 // Decode GEMMs are bound by streaming B from HBM: every SM streams an equal
 // share of B through a deep ring (128-256 KB of B in flight per SM), and a
 // stage carries up to two K blocks so one TMA request moves 32 KB of B.
-// Modes: kModePlain (alpha only) and kModeMX (UE8M0 1x32 scales; the weights'
-// scale atoms are the MMA's A scales, the activations' its B scales).
+// Modes: kModePlain (alpha only), kModeMX and kModeMX4 (E4M3 or packed E2M1 with
+// UE8M0 1x32 scales; the weights' scale atoms are the MMA's A scales, the
+// activations' its B scales).
 #pragma once
 
 #include "b2g_gemm.cuh"
@@ -41,13 +42,14 @@ struct SkinnyCfg {
   static constexpr int kABlk = kMP * 128;  // the A rows of one 128-K block
   static constexpr int kWBytes = kKB * kWBlk;
   static constexpr int kABytes = kKB * kABlk;
-  static constexpr int kSfBytes = kMode == kModeMX ? 512 * kKB : 0;  // kKB atoms each
+  static constexpr int kKAtoms = mode_atoms(kMode);        // scale K-atoms per 128-byte K block
+  static constexpr int kSfBytes = 512 * kKB * kKAtoms;      // per operand per stage
   static constexpr int kStageBytes = kWBytes + kABytes + 2 * kSfBytes;
   static constexpr int kMaxStages = kKB == 1 ? 8 : 5;
   static constexpr int kStages = 225000 / kStageBytes < kMaxStages ? 225000 / kStageBytes : kMaxStages;
   static constexpr int kAccStages = 2;
   static constexpr int kAccStride = kMP < 32 ? 32 : kMP;  // accumulator stages start 32-column aligned
-  static constexpr int kSfCols = kMode == kModeMX ? 8 : 0;  // weight atom (4) + activation atom (4)
+  static constexpr int kSfCols = 8 * kKAtoms;  // weight K-atoms (4 columns each), then activation K-atoms
   static constexpr int kSfCol = kAccStages * kAccStride;     // two alternating scale sets follow
   static constexpr int kColsUsed = kSfCol + 2 * kSfCols;
   static constexpr int kTmemCols = kColsUsed <= 32 ? 32 : kColsUsed <= 64 ? 64 : kColsUsed <= 128 ? 128
@@ -205,8 +207,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       tma_load_3d_hint(w_dst, &tm_w, &full[s], 0, nt * 128, kb, pol_w);
     else
       tma_load_3d_hint(w_dst, &tm_w, &full[s], kb * 128, nt * 128, 0, pol_w);
-    if (kMode == kModeMX)
-      bulk_load(smem + Cfg::kOffSfw + s * Cfg::kSfBytes, p.sfw + nt * p.sf_rb + kb * 512, Cfg::kSfBytes, &full[s]);
+    if (mode_mx(kMode))
+      bulk_load(smem + Cfg::kOffSfw + s * Cfg::kSfBytes, p.sfw + nt * p.sf_rb + kb * 512 * Cfg::kKAtoms, Cfg::kSfBytes,
+                &full[s]);
   };
   // the activations' part
   auto issue_a = [&](long long u, int s) {
@@ -217,8 +220,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       tma_load_3d(a_dst, &tm_a, &full[s], 0, 0, kb);
     else
       tma_load_3d(a_dst, &tm_a, &full[s], kb * 128, 0, 0);
-    if (kMode == kModeMX)
-      bulk_load(smem + Cfg::kOffSfa + s * Cfg::kSfBytes, p.sfa + kb * 512, Cfg::kSfBytes, &full[s]);
+    if (mode_mx(kMode))
+      bulk_load(smem + Cfg::kOffSfa + s * Cfg::kSfBytes, p.sfa + kb * 512 * Cfg::kKAtoms, Cfg::kSfBytes, &full[s]);
   };
   auto issue = [&](long long u, int s) {
     issue_w(u, s);
@@ -300,11 +303,15 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             const uint32_t a_base = smem_u32(smem + Cfg::kOffA + s * Cfg::kABytes + j * Cfg::kABlk);
             const uint32_t sf_off = sfbuf * Cfg::kSfCols;
             sfbuf ^= 1;
-            if (kMode == kModeMX) {
-              tc_cp_32x128b_warpx4(tmem_base + Cfg::kSfCol + sf_off,
-                                   desc_sf_atom(smem_u32(smem + Cfg::kOffSfw + s * Cfg::kSfBytes + j * 512)));
-              tc_cp_32x128b_warpx4(tmem_base + Cfg::kSfCol + sf_off + 4,
-                                   desc_sf_atom(smem_u32(smem + Cfg::kOffSfa + s * Cfg::kSfBytes + j * 512)));
+            if (mode_mx(kMode)) {
+#pragma unroll
+              for (int q = 0; q < Cfg::kKAtoms; ++q) {
+                const int at = (j * Cfg::kKAtoms + q) * 512;
+                tc_cp_32x128b_warpx4(tmem_base + Cfg::kSfCol + sf_off + 4 * q,
+                                     desc_sf_atom(smem_u32(smem + Cfg::kOffSfw + s * Cfg::kSfBytes + at)));
+                tc_cp_32x128b_warpx4(tmem_base + Cfg::kSfCol + sf_off + 4 * Cfg::kKAtoms + 4 * q,
+                                     desc_sf_atom(smem_u32(smem + Cfg::kOffSfa + s * Cfg::kSfBytes + at)));
+              }
             }
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
@@ -315,6 +322,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
               if (kMode == kModeMX)
                 mma_mxf8f6f4(d_tmem, wdesc, adesc, idesc_mxf8f6f4(128, MP, kk, kk), tmem_base + Cfg::kSfCol + sf_off,
                              tmem_base + Cfg::kSfCol + sf_off + 4, acc);
+              else if (kMode == kModeMX4)  // K-atom kk / 2, byte pair 2 * (kk % 2)
+                mma_mxf4(d_tmem, wdesc, adesc, idesc_mxf4(128, MP, (kk & 1) * 2, (kk & 1) * 2),
+                         tmem_base + Cfg::kSfCol + sf_off + 4 * (kk >> 1),
+                         tmem_base + Cfg::kSfCol + sf_off + 4 * Cfg::kKAtoms + 4 * (kk >> 1), acc);
               else
                 mma_f8f6f4(d_tmem, wdesc, adesc, idesc_f8f6f4(128, MP), acc);
             }

@@ -272,6 +272,19 @@ __device__ __forceinline__ void mma_mxf8f6f4(uint32_t d_tmem, uint64_t adesc, ui
       : "memory");
 }
 
+// kind::mxf4.block_scale.scale_vec::2X: packed E2M1 operands, K = 64 per
+// instruction (32 bytes, the same smem footprint as one 32-K E4M3 step), two
+// UE8M0 scales per row per instruction.
+__device__ __forceinline__ void mma_mxf4(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.scale_vec::2X [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
+      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
 // smem (32 rows x 16 B) -> TMEM, replicated into all four 32-lane groups.
 __device__ __forceinline__ void tc_cp_32x128b_warpx4(uint32_t taddr, uint64_t sdesc) {
   asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
@@ -360,6 +373,14 @@ __host__ __device__ constexpr uint32_t idesc_f8f6f4(uint32_t M, uint32_t N) {
 // the byte of the 32-bit TMEM scale word (the 32-K step inside a 128-K block).
 __host__ __device__ constexpr uint32_t idesc_mxf8f6f4(uint32_t M, uint32_t N, uint32_t sfa_id, uint32_t sfb_id) {
   return ((sfb_id & 3u) << 4) | (0u << 7) | (0u << 10) | ((N >> 3) << 17) | (1u << 23) | ((M >> 4) << 24) |
+         ((sfa_id & 3u) << 29);
+}
+
+// kind::mxf4.block_scale.scale_vec::2X, E2M1 x E2M1 (format 1 of the MXF4 kinds),
+// UE8M0 scales, K = 64; sfa_id / sfb_id (0 or 2) pick the byte pair of the 32-bit
+// TMEM scale word (the 64-K half of a 128-K atom).
+__host__ __device__ constexpr uint32_t idesc_mxf4(uint32_t M, uint32_t N, uint32_t sfa_id, uint32_t sfb_id) {
+  return ((sfb_id & 3u) << 4) | (1u << 7) | (1u << 10) | ((N >> 3) << 17) | (1u << 23) | ((M >> 4) << 24) |
          ((sfa_id & 3u) << 29);
 }
 
@@ -469,6 +490,16 @@ __device__ __forceinline__ void mma_mxf8f6f4_pair(uint32_t d_tmem, uint64_t ades
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
+      ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_mxf4_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf4.block_scale.scale_vec::2X [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
       ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
       : "memory");
 }

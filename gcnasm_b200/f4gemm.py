@@ -188,7 +188,9 @@ class Shape:
         return round_up(self.M, 32)
 
 
-def launch(args: capi.F4gemmKernelArgs, bpreshuffle: int, out_dtype: int = capi.OUT_BF16, stream: int = 0) -> None:
-    """Kernel::launch (asm_f4gemm/f4gemm.hpp:297-309) on this library's kernels."""
-    capi.check(capi.lib().b2g_gemm_mxfp8_f4gemm(C.byref(args), int(bpreshuffle), int(out_dtype),
-                                                 C.c_void_p(stream)), "b2g_gemm_mxfp8_f4gemm")
+def launch(args: capi.F4gemmKernelArgs, bpreshuffle: int, out_dtype: int = capi.OUT_BF16, stream: int = 0,
+           fp4: bool = False) -> None:
+    """Kernel::launch (asm_f4gemm/f4gemm.hpp:297-309) on this library's kernels: MXFP8
+    operands, or with fp4=True the reference's own MXFP4 (packed E2M1) operands."""
+    fn = "b2g_gemm_mxfp4_f4gemm" if fp4 else "b2g_gemm_mxfp8_f4gemm"
+    capi.check(getattr(capi.lib(), fn)(C.byref(args), int(bpreshuffle), int(out_dtype), C.c_void_p(stream)), fn)

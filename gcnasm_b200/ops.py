@@ -120,6 +120,23 @@ def mxfp8_gemm(a: torch.Tensor, b: torch.Tensor, sfa_tc: torch.Tensor, sfb_tc: t
     return out
 
 
+def mxfp4_gemm(a: torch.Tensor, b: torch.Tensor, sfa_tc: torch.Tensor, sfb_tc: torch.Tensor,
+               out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16, alpha: float = 1.0,
+               b_preshuffled: bool = False, log2_k_split: int = 0, stream=None) -> torch.Tensor:
+    """D[M, N] = alpha * A . B^T with MXFP4 operands (b2g_gemm_mxfp4): a [M, K/2] and
+    b [N, K/2] uint8 of packed E2M1 (element 2i in the low nibble), scales in the
+    tensor-core atom layout for K elements."""
+    m, kh = a.shape
+    n = b.shape[0]
+    if out is None:
+        out = torch.empty((m, n), dtype=out_dtype, device=a.device)
+    args = capi.Mxfp8Args(a.data_ptr(), b.data_ptr(), sfa_tc.data_ptr(), sfb_tc.data_ptr(), out.data_ptr(),
+                          m, n, 2 * kh, 2 * a.stride(0), 2 * kh if b_preshuffled else 2 * b.stride(0),
+                          out.stride(0), alpha, int(b_preshuffled), _out_code(out.dtype), log2_k_split)
+    capi.check(capi.lib().b2g_gemm_mxfp4(C.byref(args), _stream(stream)), "b2g_gemm_mxfp4")
+    return out
+
+
 def set_static_weights(on: bool) -> None:
     """b2g_set_static_weights: let decode GEMMs (M <= 128) read B and its scales
     before the preceding kernel on the stream completes (weights no kernel writes)."""

@@ -5,7 +5,7 @@ launches and report TFLOP/s (opus_gemm/block_scale_gemm/gemm_a8w8_blockscale_hos
 block_scale_1x128x1 adds BENCH_WARMUP / BENCH_ITERS / BENCH_ROUNDS and reports the
 best / median / worst round (block_scale_1x128x1_gemm/..._host.cc:103-154); f4gemm
 takes -m -n -k --splitk --bpreshuffle --iters (asm_f4gemm/main.cpp:32-109).  This
-harness keeps those flags and environment knobs, adds the mode (mx | blk | plain),
+harness keeps those flags and environment knobs, adds the mode (mx | mx4 | blk | plain),
 and with --sweep times every manifest tile x split candidate and writes a CSV
 tuning table (tile choice per shape).
 
@@ -27,6 +27,16 @@ from . import capi, ops
 
 def operands(mode, M, N, K, dev, group_n=128, bpre=False):
     g = torch.Generator(device=dev)
+    if mode == "mx4":
+        # the f4gemm data recipe (asm_f4gemm/f4gemm_ref.hpp:150-177): uniform E2M1 nibbles,
+        # UE8M0 exponents 124..130
+        qa = torch.randint(0, 256, (M, K // 2), dtype=torch.uint8, device=dev, generator=g.manual_seed(1234))
+        qb = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=dev, generator=g.manual_seed(5678))
+        sa = torch.randint(124, 131, (M, K // 32), dtype=torch.uint8, device=dev, generator=g.manual_seed(11))
+        sb = torch.randint(124, 131, (N, K // 32), dtype=torch.uint8, device=dev, generator=g.manual_seed(12))
+        if bpre:
+            qb = ops.shuffle_weight_16x16(qb)
+        return qa, qb, ops.sf_rowmajor_to_tc(sa, K), ops.sf_rowmajor_to_tc(sb, K)
     x = torch.randn(M, K, device=dev, generator=g.manual_seed(1234))
     w = torch.randn(N, K, device=dev, generator=g.manual_seed(5678))
     if mode == "mx":
@@ -50,6 +60,8 @@ def make_call(mode, ab, out, log2, group_n=128, bpre=False):
     qa, qb, sfa, sfb = ab
     if mode == "mx":
         return lambda: ops.mxfp8_gemm(qa, qb, sfa, sfb, out=out, log2_k_split=log2, b_preshuffled=bpre)
+    if mode == "mx4":
+        return lambda: ops.mxfp4_gemm(qa, qb, sfa, sfb, out=out, log2_k_split=log2, b_preshuffled=bpre)
     if mode == "blk":
         return lambda: ops.gemm_a8w8_blockscale(qa, qb, sfa, sfb, group_n=group_n, out=out, log2_k_split=log2)
     return lambda: ops.gemm_a8w8(qa, qb, out=out, log2_k_split=log2, b_preshuffled=bpre)
@@ -139,6 +151,8 @@ def time_rounds(fn, warmup, iters, rounds, flush_bytes=0, graph=False):
 def algorithmic_bytes(mode, M, N, K, out_bytes, group_n=128):
     if mode == "mx":
         return M * K + N * K + (M + N) * (K // 32) + out_bytes * M * N
+    if mode == "mx4":
+        return (M * K + N * K) // 2 + (M + N) * (K // 32) + out_bytes * M * N
     if mode == "blk":
         sfb = (N // 128) * (K // 128) if group_n == 128 else N * (K // 128)
         return M * K + N * K + 4 * M * (K // 128) + 4 * sfb + out_bytes * M * N
@@ -148,7 +162,7 @@ def algorithmic_bytes(mode, M, N, K, out_bytes, group_n=128):
 def main(argv=None):
     env = os.environ
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("--mode", choices=["mx", "blk", "plain"], default="mx")
+    ap.add_argument("--mode", choices=["mx", "mx4", "blk", "plain"], default="mx")
     ap.add_argument("-m", type=int, default=8192)
     ap.add_argument("-n", type=int, default=8192)
     ap.add_argument("-k", type=int, default=8192)

@@ -166,6 +166,17 @@ typedef struct B2G_PACKED b2g_f4gemm_kargs {
  * Contract: K % 32 == 0, N % 16 == 0. */
 B2G_API int b2g_gemm_mxfp8_f4gemm(const b2g_f4gemm_kargs* args, int bpreshuffle, int out_dtype, void* stream);
 
+/* The same entry with MXFP4 operands: the reference's own f4gemm element type.
+ * A [M, K/2] and B [N, K/2] hold packed OCP E2M1, element 2i in the low nibble
+ * of byte i (asm_f4gemm/f4gemm_ref.hpp:22-26); one UE8M0 scale per 1x32 block of
+ * K, padded + shuffled as for MXFP8.  stride_A0 / stride_B0 count E2M1 elements
+ * (fill_args sets them to K: f4gemm.hpp:351-353), so a row is stride/2 bytes;
+ * bpreshuffle = 1 takes B through shuffle_weight_16x16 over its bytes
+ * (f4gemm_ref.hpp:78-96), as the reference kernels do.  alpha, beta/C, the K
+ * split and the output types behave as in b2g_gemm_mxfp8_f4gemm.
+ * Contract: K % 256 == 0 (asm_f4gemm/main.cpp:141-150), N % 16 == 0. */
+B2G_API int b2g_gemm_mxfp4_f4gemm(const b2g_f4gemm_kargs* args, int bpreshuffle, int out_dtype, void* stream);
+
 /* Native MXFP8 entry: scales already in the sm_100 tensor-core atom layout
  * (b2g_sf_tc_bytes / b2g_sf_rowmajor_to_tc), so no per-call layout work.
  * ld* in elements.  b_preshuffled: B in the 16x16 preshuffled layout. */
@@ -184,6 +195,12 @@ typedef struct b2g_mxfp8_args {
 } b2g_mxfp8_args;
 
 B2G_API int b2g_gemm_mxfp8(const b2g_mxfp8_args* args, void* stream);
+
+/* Native MXFP4 entry over the same argument block: a, b packed E2M1 (two per byte,
+ * element 2i in the low nibble), scales in the tensor-core atom layout for K
+ * elements (b2g_sf_tc_bytes(rows, k)).  k, lda and ldb count E2M1 elements (even;
+ * a row is ld/2 bytes); K % 256 == 0. */
+B2G_API int b2g_gemm_mxfp4(const b2g_mxfp8_args* args, void* stream);
 
 /* Column-parallel MXFP8 GEMM for one GPU of a multi-GPU job with the output
  * all-gather folded into the epilogue (no counterpart in the reference, whose

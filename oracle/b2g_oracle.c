@@ -414,6 +414,47 @@ ORC_API void orc_gemm_mx(const uint8_t* a, const uint8_t* b, const uint8_t* sfa,
     }
 }
 
+/* MXFP4 (OCP e2m1) element decode: the nibble -> value table of
+ * asm_f4gemm/f4gemm_ref.hpp:24-26.  Byte i of a packed row holds element 2i in
+ * its low nibble and element 2i+1 in its high nibble (f4gemm_ref.hpp:22-23). */
+static const float k_e2m1[16] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f,
+                                 -0.0f, -0.5f, -1.0f, -1.5f, -2.0f, -3.0f, -4.0f, -6.0f};
+
+ORC_API float orc_e2m1_to_f32(uint8_t nib) { return k_e2m1[nib & 15]; }
+
+/* MXFP4 reference GEMM, the f4gemm path itself: every element dequantised as
+ * e2m1(nibble) * 2^(e-127) (make_operand, f4gemm_ref.hpp:150-177), then
+ * D = alpha * A.B^T accumulated in f64 like reference_gemm (f4gemm_ref.hpp:181-222)
+ * when acc_f64 = 1, or in fp32.  a/b are packed [rows][lda_bytes] with K
+ * elements per row (K even); sfa/sfb plain row-major [rows][sf_ld] UE8M0. */
+ORC_API void orc_gemm_mxfp4(const uint8_t* a, const uint8_t* b, const uint8_t* sfa, const uint8_t* sfb,
+                            int m, int n, int k, int lda_bytes, int ldb_bytes, int sfa_ld, int sfb_ld,
+                            float alpha, int acc_f64, float* d, int ldd)
+{
+#pragma omp parallel for collapse(2) schedule(static)
+    for (int i = 0; i < m; ++i) {
+        for (int j = 0; j < n; ++j) {
+            const uint8_t* ar = a + (int64_t)i * lda_bytes;
+            const uint8_t* br = b + (int64_t)j * ldb_bytes;
+            double acc64 = 0.0;
+            float acc32 = 0.0f;
+            for (int p0 = 0; p0 < k; p0 += 32) {
+                const float s_a = orc_e8m0_to_f32(sfa[(int64_t)i * sfa_ld + p0 / 32]);
+                const float s_b = orc_e8m0_to_f32(sfb[(int64_t)j * sfb_ld + p0 / 32]);
+                const int p1 = p0 + 32 < k ? p0 + 32 : k;
+                for (int p = p0; p < p1; ++p) {
+                    const uint8_t ba = ar[p >> 1], bb = br[p >> 1];
+                    const float va = k_e2m1[(p & 1) ? (ba >> 4) : (ba & 15)] * s_a;  /* exact */
+                    const float vb = k_e2m1[(p & 1) ? (bb >> 4) : (bb & 15)] * s_b;
+                    if (acc_f64) acc64 += (double)va * (double)vb;
+                    else acc32 += va * vb;
+                }
+            }
+            d[(int64_t)i * ldd + j] = acc_f64 ? alpha * (float)acc64 : alpha * acc32;
+        }
+    }
+}
+
 /* ------------------------------------------------------------------------- */
 /* Layout transforms                                                         */
 /* ------------------------------------------------------------------------- */

@@ -64,6 +64,8 @@ def lib() -> C.CDLL:
         L.orc_gemm_a8w8.argtypes = [u8p, u8p, f32p] + [ci] * 6
         L.orc_gemm_a8w8_kn.argtypes = [u8p, u8p, f32p] + [ci] * 6
         L.orc_gemm_mx.argtypes = [u8p, u8p, u8p, u8p] + [ci] * 7 + [C.c_float, ci, f32p, ci]
+        L.orc_gemm_mxfp4.argtypes = [u8p, u8p, u8p, u8p] + [ci] * 7 + [C.c_float, ci, f32p, ci]
+        L.orc_e2m1_to_f32.argtypes = [C.c_uint8]; L.orc_e2m1_to_f32.restype = C.c_float
         L.orc_shuffle_weight_16x16.argtypes = [u8p, u8p, ci, ci]
         L.orc_shuffle_scale.argtypes = [u8p, ci, ci, ci, ci, u8p]
         L.orc_flatmm_shuffle_b.argtypes = [u8p, u8p, ci, ci]
@@ -202,6 +204,40 @@ def gemm_mx(a, b, sfa, sfb, m, n, k, alpha=1.0, acc_f64=True):
                       np.ascontiguousarray(sfb), m, n, k, a.shape[1], b.shape[1], sfa.shape[1], sfb.shape[1],
                       float(alpha), int(acc_f64), d, n)
     return d
+
+
+def gemm_mxfp4(a, b, sfa, sfb, m, n, k, alpha=1.0, acc_f64=True):
+    """MXFP4 reference GEMM (asm_f4gemm/f4gemm_ref.hpp:181-222) on packed e2m1
+    operands [rows][K/2 bytes] with UE8M0 scales [rows][>= K/32]."""
+    d = np.empty((m, n), dtype=np.float32)
+    lib().orc_gemm_mxfp4(np.ascontiguousarray(a), np.ascontiguousarray(b), np.ascontiguousarray(sfa),
+                         np.ascontiguousarray(sfb), m, n, k, a.shape[1], b.shape[1], sfa.shape[1], sfb.shape[1],
+                         float(alpha), int(acc_f64), d, n)
+    return d
+
+
+E2M1 = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0, -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0],
+                dtype=np.float32)
+
+
+def e2m1_decode(packed: np.ndarray) -> np.ndarray:
+    """Packed e2m1 bytes [rows][K/2] -> fp32 [rows][K], element 2i from the low nibble."""
+    p = np.asarray(packed, dtype=np.uint8)
+    out = np.empty(p.shape[:-1] + (p.shape[-1] * 2,), dtype=np.float32)
+    out[..., 0::2] = E2M1[p & 15]
+    out[..., 1::2] = E2M1[p >> 4]
+    return out
+
+
+def fp4_operand(rows: int, K: int, seed: int):
+    """Random MXFP4 operand with the reference's data recipe (make_operand,
+    f4gemm_ref.hpp:150-177): uniform nibbles 0..15 and UE8M0 exponents 124..130
+    (2^-3 .. 2^3); numpy's generator stands in for std::mt19937.  Returns
+    (packed [rows][K/2] uint8, scales [rows][K/32] uint8)."""
+    rs = np.random.RandomState(seed)
+    packed = rs.randint(0, 256, size=(rows, K // 2)).astype(np.uint8)
+    scales = rs.randint(124, 131, size=(rows, K // 32)).astype(np.uint8)
+    return packed, scales
 
 
 # --------------------------------------------------------------------------- layouts

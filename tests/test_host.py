@@ -200,6 +200,24 @@ def test_peer_out_validation_without_gpu():
     assert b"peer" in L.b2g_last_error()
 
 
+def test_mxfp4_validation_without_gpu():
+    """MXFP4 entries refuse K off the 256-element granule (the reference's f4gemm
+    contract, asm_f4gemm/main.cpp:141-150) and odd element strides before any
+    device work (fake, never dereferenced pointers)."""
+    from gcnasm_b200 import f4gemm
+    L = capi.lib()
+    args = capi.Mxfp8Args(0x10000, 0x20000, 0x30000, 0x40000, 0x50000, 256, 1024, 1152, 1152, 1152, 1024, 1.0, 0,
+                          capi.OUT_BF16, 0)
+    assert L.b2g_gemm_mxfp4(C.byref(args), None) == capi.B2G_ERR_UNSUPPORTED  # K = 1152: not a multiple of 256
+    args = capi.Mxfp8Args(0x10000, 0x20000, 0x30000, 0x40000, 0x50000, 256, 1024, 1024, 1025, 1024, 1024, 1.0, 0,
+                          capi.OUT_BF16, 0)
+    assert L.b2g_gemm_mxfp4(C.byref(args), None) == capi.B2G_ERR_ALIGNMENT  # odd element stride
+    a = f4gemm.fill_args(0x50000, None, 0x10000, 0x20000, 0x30000, 0x40000, 256, 1024, 1056, 1024, 40, 40,
+                         1.0, 0.0, 0)
+    assert L.b2g_gemm_mxfp4_f4gemm(C.byref(a), 1, capi.OUT_BF16, None) == capi.B2G_ERR_UNSUPPORTED
+    assert b"256" in L.b2g_last_error()
+
+
 def test_sf_tc_bytes():
     L = capi.lib()
     assert L.b2g_sf_tc_bytes(8192, 8192) == 64 * 64 * 512

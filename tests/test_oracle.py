@@ -108,6 +108,34 @@ def test_reference_gemm_f64_matches_reference(oracle, golden):
     assert np.array_equal(mine, ref)
 
 
+def test_mxfp4_oracle_matches_reference_golden(oracle, golden):
+    # the reference's own MXFP4 operands (make_operand, f4gemm_ref.hpp:150-177):
+    # the oracle's e2m1 decode reproduces its dequantised values and the oracle's
+    # f64 GEMM over the packed bytes reproduces reference_gemm (f4gemm_ref.hpp:181-222)
+    pa = golden["op_a_packed"].reshape(8, 32)
+    sa = golden["op_a_scales"].reshape(8, 2)
+    pb = golden["op_b_packed"].reshape(4, 32)
+    sb = golden["op_b_scales"].reshape(4, 2)
+    da = oracle.e2m1_decode(pa) * np.repeat(oracle.e8m0_decode(sa), 32, axis=1)
+    db = oracle.e2m1_decode(pb) * np.repeat(oracle.e8m0_decode(sb), 32, axis=1)
+    assert np.array_equal(da, golden["op_a_dequant"].reshape(8, 64))
+    assert np.array_equal(db, golden["op_b_dequant"].reshape(4, 64))
+    d = oracle.gemm_mxfp4(pa, pb, sa, sb, 8, 4, 64, acc_f64=True)
+    assert np.array_equal(d, golden["ref_gemm_D"].reshape(8, 4))
+    assert [oracle.lib().orc_e2m1_to_f32(i) for i in range(16)] == list(oracle.E2M1)
+
+
+def test_mxfp4_oracle_f32_close_to_f64(oracle):
+    pa, sa = oracle.fp4_operand(24, 512, 1)
+    pb, sb = oracle.fp4_operand(40, 512, 2)
+    f64 = oracle.gemm_mxfp4(pa, pb, sa, sb, 24, 40, 512, acc_f64=True)
+    f32 = oracle.gemm_mxfp4(pa, pb, sa, sb, 24, 40, 512, acc_f64=False)
+    da = oracle.e2m1_decode(pa).astype(np.float64) * np.repeat(oracle.e8m0_decode(sa), 32, axis=1)
+    db = oracle.e2m1_decode(pb).astype(np.float64) * np.repeat(oracle.e8m0_decode(sb), 32, axis=1)
+    np.testing.assert_allclose(f64, da @ db.T, rtol=1e-6, atol=1e-6)
+    assert oracle.check_f32(f32, f64) < 1e-5
+
+
 def test_gemm_mx_oracle_consistent(oracle):
     x = oracle.normal_rows(1234, 0, 32, 128)
     w = oracle.normal_rows(5678, 0, 48, 128)
