@@ -249,6 +249,8 @@ def run_b200(args, rank, world, local_rank):
 
     # ---------------------------------------------------------------- decode config (HBM-bound)
     result["decode"] = bench_decode(args, dev, stream, peaks, flush)
+    # ---------------------------------------------------------------- MXFP4 (the f4gemm element type)
+    result["mxfp4"] = bench_mxfp4(args, dev, stream, peaks, flush)
     # ---------------------------------------------------------------- CPU baseline (oracle port, N=1)
     if world == 1:
         tf, rows, cores, secs = cpu_gemm_sample(M, N, K, budget_s=args.cpu_budget)
@@ -425,6 +427,47 @@ def bench_decode(args, dev, stream, peaks, flush):
                                "frac": round(nbytes / (ms_s * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
                                "note": "b2g_set_static_weights(1): B and its scales may be read before the "
                                        "preceding call completes (serving loop with fixed weights)"}}
+
+
+def bench_mxfp4(args, dev, stream, peaks, flush):
+    """MXFP4 8192^3 (packed E2M1 A/B, UE8M0 1x32 scales, bf16 C): the reference
+    f4gemm's own element type on the same CTA-pair kernel with tcgen05
+    kind::mxf4.  Operands follow the f4gemm data recipe (f4gemm_ref.hpp:150-177:
+    uniform nibbles, exponents 124..130).  Roofline: tcgen05 FP4 runs at 4x the
+    measured dense bf16 rate."""
+    import torch
+
+    from gcnasm_b200 import ops
+
+    M = N = K = 8192
+    g = torch.Generator(device=dev)
+    qa = torch.randint(0, 256, (M, K // 2), dtype=torch.uint8, device=dev, generator=g.manual_seed(41))
+    qb = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device=dev, generator=g.manual_seed(42))
+    sa = torch.randint(124, 131, (M, K // 32), dtype=torch.uint8, device=dev, generator=g.manual_seed(43))
+    sb = torch.randint(124, 131, (N, K // 32), dtype=torch.uint8, device=dev, generator=g.manual_seed(44))
+    sfa, sfb = ops.sf_rowmajor_to_tc(sa, K), ops.sf_rowmajor_to_tc(sb, K)
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+
+    def step():
+        ops.mxfp4_gemm(qa, qb, sfa, sfb, out=out, stream=stream)
+
+    step()
+    torch.cuda.synchronize()
+    times = timed_steps(step, max(args.steps // 2, 10), 3, flush, stream)
+    ms = statistics.mean(times)
+    tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+    peak = 4.0 * peaks["bf16_tflops"]
+    del qa, qb, sfa, sfb, out
+    torch.cuda.empty_cache()
+    return {"M": M, "N": N, "K": K, "out": "bf16", "ms_per_call": round(ms, 4), "value": round(tf, 2),
+            "unit": "TFLOP/s", "dtype": "e2m1+ue8m0 (fp32 accumulate), bf16 out",
+            "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": round(peak, 1), "unit": "TFLOP/s",
+                         "frac": round(tf / peak, 4),
+                         "peak_source": f"{peaks['source']} bf16 dense x4 (tcgen05 FP4 rate = 4x bf16)",
+                         "frac_of_nominal_9000": round(tf / 9000.0, 4),
+                         "traffic": load_traffic().get("mxfp4_8192_gemm_bytes"),
+                         "kernel": "b2g_gemm_pair_kernel<PairCfg<MX4,256>>"},
+            "gpu_launches_per_call": 1}
 
 
 def bench_e2e(args, dev, stream, qa, sfa_rm, qb, sfb_rm, M, N, K):
