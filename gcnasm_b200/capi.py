@@ -33,7 +33,7 @@ OUT_F32 = 1
 # every symbol include/b2g/gemm.h declares
 EXPORTS = [
     "b2g_gemm_a8w8_blockscale", "b2g_gemm_a8w8", "b2g_gemm_a8w8_preshuffled", "b2g_gemm_mxfp8_f4gemm",
-    "b2g_gemm_mxfp4_f4gemm", "b2g_gemm_mxfp8", "b2g_gemm_mxfp4", "b2g_gemm_mxfp8_peer_out", "b2g_set_static_weights", "b2g_gemm_mxfp8_noalloc", "b2g_select", "b2g_manifest_size", "b2g_manifest_entry", "b2g_sf_tc_bytes",
+    "b2g_gemm_mxfp4_f4gemm", "b2g_gemm_mxfp8", "b2g_gemm_mxfp4", "b2g_gemm_mxfp8_ex", "b2g_gemm_mxfp4_ex", "b2g_gemm_mxfp8_peer_out", "b2g_set_static_weights", "b2g_gemm_mxfp8_noalloc", "b2g_select", "b2g_manifest_size", "b2g_manifest_entry", "b2g_sf_tc_bytes",
     "b2g_sf_rowmajor_to_tc", "b2g_sf_f4gemm_to_tc", "b2g_shuffle_scale", "b2g_shuffle_weight_16x16",
     "b2g_unshuffle_weight_16x16", "b2g_quant_mxfp8", "b2g_quant_1x128", "b2g_quant_128x128",
     "b2g_device_status", "b2g_set_wait_timeout_ms", "b2g_debug_force_stall", "b2g_status_string",
@@ -99,6 +99,11 @@ class Mxfp8Args(C.Structure):
     ]
 
 
+class Epilogue(C.Structure):
+    """b2g_epilogue: D = alpha * A . B^T + beta * C + bias[n] (C, bias in D's type)."""
+    _fields_ = [("c", C.c_void_p), ("ldc", C.c_longlong), ("beta", C.c_float), ("bias", C.c_void_p)]
+
+
 _LIB = None
 
 
@@ -116,6 +121,8 @@ def lib() -> C.CDLL:
         L.b2g_gemm_mxfp8_f4gemm.argtypes = [C.POINTER(F4gemmKernelArgs), ci, ci, vp]
         L.b2g_gemm_mxfp8.argtypes = [C.POINTER(Mxfp8Args), vp]
         L.b2g_gemm_mxfp4.argtypes = [C.POINTER(Mxfp8Args), vp]
+        L.b2g_gemm_mxfp8_ex.argtypes = [C.POINTER(Mxfp8Args), C.POINTER(Epilogue), vp]
+        L.b2g_gemm_mxfp4_ex.argtypes = [C.POINTER(Mxfp8Args), C.POINTER(Epilogue), vp]
         L.b2g_gemm_mxfp4_f4gemm.argtypes = [C.POINTER(F4gemmKernelArgs), ci, ci, vp]
         L.b2g_gemm_mxfp8_noalloc.argtypes = [C.POINTER(Mxfp8Args), vp]
         L.b2g_set_static_weights.argtypes = [ci]

@@ -305,6 +305,8 @@ struct Req {
   void* const* peer_c = nullptr;
   int n_peers = 0, peer_self = 0;
   long long peer_ldc = 0, peer_col0 = 0;
+  // beta * C and a per-column bias (b2g_epilogue), in the output's element type
+  EpiTerms epi = {};
 };
 
 template <class Cfg>
@@ -321,6 +323,19 @@ int launch_cfg(const Env& d, const CUtensorMap& ta, const CUtensorMap& tb, const
 template <int kMode, int kBN>
 int dispatch_pre_out(const Env& d, bool pre, bool f32, const CUtensorMap& ta, const CUtensorMap& tb,
                      const GemmParams& p, int grid, cudaStream_t st) {
+  // beta * C / bias in the epilogue: separate instances (MX modes, 256-wide tiles),
+  // so the kernels without the terms compile exactly as before
+  if constexpr (mode_mx(kMode) && kBN == 256) {
+    if (epi_any(p.epi) && p.out_mode == kOutStore) {
+      if (pre)
+        return f32 ? launch_cfg<GemmCfg<kMode, 256, true, true, true>>(d, ta, tb, p, grid, st)
+                   : launch_cfg<GemmCfg<kMode, 256, true, false, true>>(d, ta, tb, p, grid, st);
+      return f32 ? launch_cfg<GemmCfg<kMode, 256, false, true, true>>(d, ta, tb, p, grid, st)
+                 : launch_cfg<GemmCfg<kMode, 256, false, false, true>>(d, ta, tb, p, grid, st);
+    }
+  }
+  if (epi_any(p.epi) && p.out_mode == kOutStore)
+    return fail(B2G_ERR_UNSUPPORTED, "beta * C / bias epilogue: MX modes with 256-wide tiles only");
   if (kMode == kModeBlk) {  // blockwise path: row-major B only
     return f32 ? launch_cfg<GemmCfg<kMode, kBN, false, true>>(d, ta, tb, p, grid, st)
                : launch_cfg<GemmCfg<kMode, kBN, false, false>>(d, ta, tb, p, grid, st);
@@ -371,6 +386,21 @@ int launch_pair(const Env& d, const CUtensorMap& ta, const CUtensorMap& tb, cons
 int dispatch_pair(const Env& d, int mode, int bn, bool pre, bool f32, const CUtensorMap& ta, const CUtensorMap& tb,
                   const CUtensorMap& tsa, const CUtensorMap& tsb, const PairParams& pp, cudaStream_t st) {
   if (bn != 256) return fail(B2G_ERR_UNSUPPORTED, "no pair kernel of width %d", bn);
+  if (epi_any(pp.g.epi) && pp.g.out_mode == kOutStore) {  // instances with the beta * C / bias terms
+    if (mode == kModeMX4) {
+      if (pre) return f32 ? launch_pair<PairCfg<kModeMX4, 256, true, true, true>>(d, ta, tb, tsa, tsb, pp, st)
+                          : launch_pair<PairCfg<kModeMX4, 256, true, false, true>>(d, ta, tb, tsa, tsb, pp, st);
+      return f32 ? launch_pair<PairCfg<kModeMX4, 256, false, true, true>>(d, ta, tb, tsa, tsb, pp, st)
+                 : launch_pair<PairCfg<kModeMX4, 256, false, false, true>>(d, ta, tb, tsa, tsb, pp, st);
+    }
+    if (mode == kModeMX) {
+      if (pre) return f32 ? launch_pair<PairCfg<kModeMX, 256, true, true, true>>(d, ta, tb, tsa, tsb, pp, st)
+                          : launch_pair<PairCfg<kModeMX, 256, true, false, true>>(d, ta, tb, tsa, tsb, pp, st);
+      return f32 ? launch_pair<PairCfg<kModeMX, 256, false, true, true>>(d, ta, tb, tsa, tsb, pp, st)
+                 : launch_pair<PairCfg<kModeMX, 256, false, false, true>>(d, ta, tb, tsa, tsb, pp, st);
+    }
+    return fail(B2G_ERR_UNSUPPORTED, "beta * C / bias epilogue: MX modes only");
+  }
   if (mode == kModeMX4) {
     if (pre) return f32 ? launch_pair<PairCfg<kModeMX4, 256, true, true>>(d, ta, tb, tsa, tsb, pp, st)
                         : launch_pair<PairCfg<kModeMX4, 256, true, false>>(d, ta, tb, tsa, tsb, pp, st);
@@ -487,7 +517,9 @@ size_t split_ws_bytes(const Req& r, int S, int sms) {
     const long long grid = std::min<long long>(skinny_units(r), sms);
     return static_cast<size_t>(2 * grid) * skinny_mp(r.M) * 128 * 4;
   }
-  return (S > 1 && !r.out_f32) ? static_cast<size_t>(S) * r.batch * r.M * r.N * 4 : 0;
+  // fp32 output adds its split-K partials into C in place, unless the epilogue has
+  // beta * C or bias terms: those go through the workspace and the reduce
+  return (S > 1 && (!r.out_f32 || epi_any(r.epi))) ? static_cast<size_t>(S) * r.batch * r.M * r.N * 4 : 0;
 }
 
 template <class Cfg>
@@ -581,6 +613,7 @@ int run_skinny(const Req& r, const Env& d) {
   sp.ldo = r.ldc;
   sp.out_f32 = r.out_f32 ? 1 : 0;
   sp.alpha = r.alpha;
+  sp.epi = r.epi;
   sp.sfw = r.sfb;
   sp.sfa = r.sfa;
   sp.sf_rb = sf_row_block_bytes(r);
@@ -710,6 +743,15 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
   if (r.ldc < r.N || (r.ldc * esz) % 16) return fail(B2G_ERR_ALIGNMENT, "C row stride %lld must be >= N and 16-byte aligned", r.ldc);
   if (r.batch > 1 && (r.a_bstride % 16 || r.b_bstride % 16 || (r.c_bstride * esz) % 16))
     return fail(B2G_ERR_ALIGNMENT, "batch strides must be 16-byte multiples");
+  if (epi_any(r.epi)) {
+    if (!mode_mx(r.mode)) return fail(B2G_ERR_UNSUPPORTED, "beta * C / bias terms: MX modes only");
+    if (r.n_peers) return fail(B2G_ERR_UNSUPPORTED, "the peer-store output takes no beta or bias term");
+    if (r.epi.cin && (!aligned16(r.epi.cin) || r.epi.ldcin < r.N || (r.epi.ldcin * esz) % 16 ||
+                      (r.batch > 1 && (r.epi.cin_bstride * esz) % 16)))
+      return fail(B2G_ERR_ALIGNMENT, "C input needs a 16-byte aligned base, row pitch >= N and whole 16-byte pitches");
+    if (r.epi.bias && (!aligned16(r.epi.bias) || (r.epi.bias_bstride * esz) % 16))
+      return fail(B2G_ERR_ALIGNMENT, "bias needs a 16-byte aligned base and batch stride");
+  }
   if (mode_mx(r.mode)) {
     if (!r.sfa || !r.sfb) return fail(B2G_ERR_INVALID_ARG, "null scale pointer");
     if (!aligned16(r.sfa) || !aligned16(r.sfb) || r.sfa_bstride % 16 || r.sfb_bstride % 16)
@@ -741,6 +783,8 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
   int bn = 0, S = 1, kb_per = 1, bm = 128;
   rc = plan_tiles(r, d.sms, &bn, &S, &kb_per, &bm);
   if (rc) return rc;
+  // the epilogue-term kernels are compiled for 256-wide tiles (unsplit calls)
+  if (epi_any(r.epi) && S == 1 && bm != 256) bn = 256;
   const bool pair = bm == 256;
   const int KB = cdiv(r.K, 128);
 
@@ -749,6 +793,7 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
   p.M = r.M; p.N = r.N; p.K = r.K; p.batch = r.batch;
   p.c = r.c; p.ldc = r.ldc; p.c_bstride = r.c_bstride;
   p.alpha = r.alpha;
+  p.epi = r.epi;
   p.sfa = r.sfa; p.sfb = r.sfb;
   p.sfa_rb = sf_row_block_bytes(r);
   p.sfb_rb = p.sfa_rb;
@@ -778,7 +823,7 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
     p.peer_col0 = r.peer_col0;
   } else if (S == 1) {
     p.out_mode = kOutStore;
-  } else if (r.out_f32) {
+  } else if (r.out_f32 && !epi_any(r.epi)) {
     p.out_mode = kOutAtomic;
   } else {
     p.out_mode = kOutWorkspace;
@@ -878,9 +923,11 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
     const long long work = static_cast<long long>(r.batch) * r.M * (r.N / 4);
     const int g = grid_for(work, 256, d.sms);
     if (r.out_f32)
-      b2g_splitk_reduce_kernel<true><<<g, 256, 0, r.stream>>>(p.ws, r.c, S, r.batch, r.M, r.N, r.ldc, r.c_bstride);
+      b2g_splitk_reduce_kernel<true><<<g, 256, 0, r.stream>>>(p.ws, r.c, S, r.batch, r.M, r.N, r.ldc, r.c_bstride,
+                                                               r.epi);
     else
-      b2g_splitk_reduce_kernel<false><<<g, 256, 0, r.stream>>>(p.ws, r.c, S, r.batch, r.M, r.N, r.ldc, r.c_bstride);
+      b2g_splitk_reduce_kernel<false><<<g, 256, 0, r.stream>>>(p.ws, r.c, S, r.batch, r.M, r.N, r.ldc, r.c_bstride,
+                                                                r.epi);
     B2G_CUDA(cudaGetLastError());
   }
   return maybe_sync_check();
@@ -1073,7 +1120,7 @@ long long b2g_sf_tc_bytes(int rows, int k) {
 
 // b2g_gemm_mxfp8 / b2g_gemm_mxfp4: K and the A/B strides arrive in elements; an
 // MXFP4 request carries them in bytes (two E2M1 elements per byte).
-static int run_mx_native(const b2g_mxfp8_args* g, int mode, void* stream) {
+static int run_mx_native(const b2g_mxfp8_args* g, int mode, void* stream, const b2g_epilogue* epi = nullptr) {
   if (!g) return fail(B2G_ERR_INVALID_ARG, "null args");
   if (g->out_dtype != B2G_OUT_BF16 && g->out_dtype != B2G_OUT_F32) return fail(B2G_ERR_INVALID_ARG, "bad out_dtype");
   const int per = mode == kModeMX4 ? 2 : 1;
@@ -1092,12 +1139,26 @@ static int run_mx_native(const b2g_mxfp8_args* g, int mode, void* stream) {
   r.sfb = static_cast<const uint8_t*>(g->sfb);
   r.log2_k_split = g->log2_k_split;
   r.stream = static_cast<cudaStream_t>(stream);
+  if (epi) {
+    r.epi.cin = epi->c;
+    r.epi.ldcin = epi->ldc;
+    r.epi.beta = epi->beta;
+    r.epi.bias = epi->bias;
+  }
   return run_gemm(r);
 }
 
 int b2g_gemm_mxfp8(const b2g_mxfp8_args* g, void* stream) { return run_mx_native(g, kModeMX, stream); }
 
+int b2g_gemm_mxfp8_ex(const b2g_mxfp8_args* g, const b2g_epilogue* epi, void* stream) {
+  return run_mx_native(g, kModeMX, stream, epi);
+}
+
 int b2g_gemm_mxfp4(const b2g_mxfp8_args* g, void* stream) { return run_mx_native(g, kModeMX4, stream); }
+
+int b2g_gemm_mxfp4_ex(const b2g_mxfp8_args* g, const b2g_epilogue* epi, void* stream) {
+  return run_mx_native(g, kModeMX4, stream, epi);
+}
 
 int b2g_gemm_mxfp8_peer_out(const b2g_mxfp8_args* g, void* const* peer_d, int n_peers, int self,
                             long long ldd_full, long long col_offset, void* stream) {
@@ -1173,13 +1234,14 @@ static int run_mx_f4gemm(const b2g_f4gemm_kargs* a, int bpreshuffle, int out_dty
   r.log2_k_split = a->log2_k_split;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   r.stream = st;
-  // D = alpha * A . B^T + beta * C (f4gemm_ref.hpp reference_gemm); beta is ignored
-  // without a C, as there.  With beta the GEMM writes alpha * A . B^T in fp32 to
-  // scratch and b2g_add_beta_c_kernel finishes D.
-  const bool out_f32 = r.out_f32;
+  // D = alpha * A . B^T + beta * C (f4gemm_ref.hpp reference_gemm): the beta term is
+  // added where the GEMM writes D (its epilogue, or the split-K reduce); beta is
+  // ignored without a C, as there.  C has D's type and row pitch stride_C0 (the
+  // reference kernels read stride_C0 for both) and may be D itself.
   if (with_c) {
-    r.out_f32 = true;
-    r.ldc = N;
+    r.epi.cin = a->ptr_C;
+    r.epi.ldcin = a->stride_C0;
+    r.epi.beta = a->beta;
   }
   // One scratch block for the re-laid-out scales and the split-K workspace,
   // sized before anything is written into it (growing it later would free it).
@@ -1189,9 +1251,8 @@ static int run_mx_f4gemm(const b2g_f4gemm_kargs* a, int bpreshuffle, int out_dty
   const long long tcA = b2g_sf_tc_bytes(M, K), tcB = b2g_sf_tc_bytes(N, K);
   const size_t offB = static_cast<size_t>((tcA + 255) / 256 * 256);
   const size_t offW = offB + static_cast<size_t>((tcB + 255) / 256 * 256);
-  const size_t v_bytes = with_c ? (static_cast<size_t>(M) * N * 4 + 255) / 256 * 256 : 0;  // fp32 alpha * A . B^T
   void* ws = nullptr;
-  rc = workspace(d, offW + v_bytes + split_ws_bytes(r, S, d->sms), &ws);
+  rc = workspace(d, offW + split_ws_bytes(r, S, d->sms), &ws);
   if (rc) return rc;
   uint8_t* sA = static_cast<uint8_t*>(ws);
   uint8_t* sB = sA + offB;
@@ -1201,21 +1262,8 @@ static int run_mx_f4gemm(const b2g_f4gemm_kargs* a, int bpreshuffle, int out_dty
       static_cast<const uint8_t*>(a->ptr_ScaleB), N, cols, snB, sB);
   B2G_CUDA(cudaGetLastError());
   r.sfa = sA; r.sfb = sB;
-  r.ws_offset = offW + v_bytes;
-  if (!with_c) return run_gemm(r);
-  float* v = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + offW);
-  r.c = v;
-  rc = run_gemm(r);
-  if (rc) return rc;
-  const long long work = static_cast<long long>(M) * (N / 4);
-  if (out_f32)
-    b2g_add_beta_c_kernel<true><<<grid_for(work, 256, d->sms), 256, 0, st>>>(v, M, N, a->ptr_C, a->ptr_D,
-                                                                             a->stride_C0, a->beta);
-  else
-    b2g_add_beta_c_kernel<false><<<grid_for(work, 256, d->sms), 256, 0, st>>>(v, M, N, a->ptr_C, a->ptr_D,
-                                                                              a->stride_C0, a->beta);
-  B2G_CUDA(cudaGetLastError());
-  return maybe_sync_check();
+  r.ws_offset = offW;
+  return run_gemm(r);
 }
 
 int b2g_gemm_mxfp8_f4gemm(const b2g_f4gemm_kargs* a, int bpreshuffle, int out_dtype, void* stream) {

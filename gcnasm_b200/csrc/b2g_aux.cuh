@@ -11,55 +11,19 @@
 #include <cuda_bf16.h>
 #include <cstdint>
 
+#include "b2g_epi.cuh"
+
 namespace b2g {
 
 // ---------------------------------------------------------------------------
-// split-K reduce: C[b][m][n] = cast(sum_s ws[s][b][m][n])
+// split-K reduce: C[b][m][n] = cast(sum_s ws[s][b][m][n] + beta * Cin + bias[n])
 // (opus_gemm_dist/opus_gemm_mem_gemm_a2a/include/gfx950/splitk_reduce_gfx950.cuh:68-259
-//  sums the split slices of an fp32 workspace and casts to D_OUT; N % 4 == 0 here)
+//  sums the split slices of an fp32 workspace, adds the optional per-column bias in
+//  fp32 and casts to D_OUT; N % 4 == 0 here).  Cin may be the output itself.
 // ---------------------------------------------------------------------------
-// D = v + beta * C with v = alpha * A . B^T already rounded to fp32 (the f4gemm
-// reference's `v = alpha * acc; v += beta * C`: fp32 multiply, fp32 add, one
-// rounding to D's type).  C has D's element type; C and D share the row pitch ld
-// (the reference kernel reads stride_C0 for both) and may be the same buffer.
 template <bool kOutF32>
-__global__ void b2g_add_beta_c_kernel(const float* __restrict__ v, int M, int N, const void* c, void* d,
-                                      long long ld, float beta) {
-  const long long n4 = N / 4;
-  const long long total = static_cast<long long>(M) * n4;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long m = i / n4;
-    const int col = static_cast<int>(i - m * n4) * 4;
-    const float4 x = __ldg(reinterpret_cast<const float4*>(v + m * N + col));
-    float cv[4];
-    if (kOutF32) {
-      const float4 t = *reinterpret_cast<const float4*>(static_cast<const float*>(c) + m * ld + col);
-      cv[0] = t.x; cv[1] = t.y; cv[2] = t.z; cv[3] = t.w;
-    } else {
-      const uint2 t = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(c) + m * ld + col);
-      const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(&t.x);
-      const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(&t.y);
-      cv[0] = __low2float(lo); cv[1] = __high2float(lo); cv[2] = __low2float(hi); cv[3] = __high2float(hi);
-    }
-    const float r0 = __fadd_rn(x.x, __fmul_rn(beta, cv[0])), r1 = __fadd_rn(x.y, __fmul_rn(beta, cv[1]));
-    const float r2 = __fadd_rn(x.z, __fmul_rn(beta, cv[2])), r3 = __fadd_rn(x.w, __fmul_rn(beta, cv[3]));
-    if (kOutF32) {
-      *reinterpret_cast<float4*>(static_cast<float*>(d) + m * ld + col) = make_float4(r0, r1, r2, r3);
-    } else {
-      __nv_bfloat162 lo = __floats2bfloat162_rn(r0, r1);
-      __nv_bfloat162 hi = __floats2bfloat162_rn(r2, r3);
-      uint2 pk;
-      pk.x = *reinterpret_cast<uint32_t*>(&lo);
-      pk.y = *reinterpret_cast<uint32_t*>(&hi);
-      *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(d) + m * ld + col) = pk;
-    }
-  }
-}
-
-template <bool kOutF32>
-__global__ void b2g_splitk_reduce_kernel(const float* __restrict__ ws, void* __restrict__ c, int S, int batch,
-                                         int M, int N, long long ldc, long long c_bstride) {
+__global__ void b2g_splitk_reduce_kernel(const float* __restrict__ ws, void* c, int S, int batch,
+                                         int M, int N, long long ldc, long long c_bstride, EpiTerms epi) {
   const long long n4 = N / 4;
   const long long total = static_cast<long long>(batch) * M * n4;
   const long long slice = static_cast<long long>(batch) * M * N;
@@ -75,6 +39,7 @@ __global__ void b2g_splitk_reduce_kernel(const float* __restrict__ ws, void* __r
     }
     const int b = static_cast<int>(row / M);
     const int m = static_cast<int>(row - static_cast<long long>(b) * M);
+    if (epi_any(epi)) epi_apply4<kOutF32>(epi, b, m, col, acc.x, acc.y, acc.z, acc.w);
     if (kOutF32) {
       float* dst = reinterpret_cast<float*>(c) + b * c_bstride + m * ldc + col;
       *reinterpret_cast<float4*>(dst) = acc;

@@ -35,6 +35,7 @@
 #include <cuda_bf16.h>
 #include <cstdint>
 
+#include "b2g_epi.cuh"
 #include "b2g_ptx.cuh"
 
 namespace b2g {
@@ -69,6 +70,7 @@ struct GemmParams {
   int n_peers, peer_first;  // peer_first: this GPU's index, where a tile's round of peer stores starts
   long long peer_ldc, peer_col0;
   float alpha;
+  EpiTerms epi;  // beta * C and bias, applied where C is written (kOutStore) or in the split-K reduce
   // MX: UE8M0 scales in the tensor-core atom layout (128 rows x 4 K-blocks per
   // 512-byte atom, atoms [row_block][k_block]); *_rb = bytes between row blocks
   const uint8_t* sfa;
@@ -212,9 +214,10 @@ __host__ __device__ __forceinline__ Unit decode_unit(int u, const GemmParams& p)
 }
 
 // compile-time configuration -------------------------------------------------
-template <int kMode_, int kBN_, bool kBPre_, bool kOutF32_>
+template <int kMode_, int kBN_, bool kBPre_, bool kOutF32_, bool kEpi_ = false>
 struct GemmCfg {
   static constexpr int kMode = kMode_;
+  static constexpr bool kEpi = kEpi_;  // beta * C / bias terms compiled in (only the instances that take them)
   static constexpr int kBN = kBN_;
   static constexpr bool kBPre = kBPre_;     // B given 16x16-preshuffled ([N/16][K/16][16][16] bytes)
   static constexpr bool kOutF32 = kOutF32_;
@@ -535,6 +538,14 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         if (!ok) break;
       }
 
+      if constexpr (Cfg::kEpi) {
+        if (p.out_mode == kOutStore && m < p.M) {
+#pragma unroll
+          for (int j = 0; j < NC; j += 4)
+            if (col0 + j < p.N)
+              epi_apply4<Cfg::kOutF32>(p.epi, w.b, m, col0 + j, acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+        }
+      }
       // ---- write the row segment [col0, col0 + NC) of row m
       if (p.tma_store && p.out_mode == kOutStore) {
         tma_store_rows<NC, Cfg::kOutF32>(&p.tm_c, acc, col0, w.mt * 128 + quad * 32, w.b, stage_c, lane);

@@ -28,9 +28,10 @@
 
 namespace b2g {
 
-template <int kMode_, int kBN_, bool kBPre_, bool kOutF32_>
+template <int kMode_, int kBN_, bool kBPre_, bool kOutF32_, bool kEpi_ = false>
 struct PairCfg {
   static constexpr int kMode = kMode_;
+  static constexpr bool kEpi = kEpi_;  // beta * C / bias terms compiled in (only the instances that take them)
   static constexpr bool kBPre = kBPre_;
   static constexpr bool kOutF32 = kOutF32_;
   static constexpr int kBN = kBN_;        // pair tile N (MMA N): 256 or 192
@@ -271,6 +272,14 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       float acc[NC];
 #pragma unroll
       for (int j = 0; j < NC; ++j) acc[j] = __uint_as_float(v[j]) * p.alpha;
+      if constexpr (Cfg::kEpi) {
+        if (p.out_mode == kOutStore && m < p.M) {
+#pragma unroll
+          for (int j = 0; j < NC; j += 4)
+            if (col0 + j < p.N)
+              epi_apply4<Cfg::kOutF32>(p.epi, w.b, m, col0 + j, acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+        }
+      }
       if (p.tma_store && p.out_mode == kOutStore) {
         tma_store_rows<NC, Cfg::kOutF32>(&p.tm_c, acc, col0, w.mt * 256 + static_cast<int>(rank) * 128 + quad * 32, w.b, stage_c, lane);
       } else if (p.out_mode == kOutPeers) {

@@ -98,6 +98,7 @@ struct SkinnyParams {
   unsigned long long timeout_ns;
   int debug_stall;
   int w_early;  // read B and its scales before the preceding kernel completes (static weights)
+  EpiTerms epi;  // beta * C and bias (C and the bias in the output type)
 };
 
 // CTA owning unit u when U units are split evenly over G CTAs (the largest c
@@ -412,7 +413,15 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       // output columns [mc, mc + CH) of this thread's output column n
       auto store_out = [&](int mc, const float (&x)[CH]) {
         if (!col_ok) return;
-        if (p.out_f32) {
+        if (epi_any(p.epi)) {
+#pragma unroll
+          for (int i = 0; i < CH; ++i)
+            if (mc + i < p.M) {
+              const float y = epi_apply1(p.epi, __fmul_rn(x[i], p.alpha), mc + i, n, p.out_f32 != 0);
+              if (p.out_f32) static_cast<float*>(p.out)[(mc + i) * p.ldo + n] = y;
+              else static_cast<__nv_bfloat16*>(p.out)[(mc + i) * p.ldo + n] = __float2bfloat16_rn(y);
+            }
+        } else if (p.out_f32) {
           float* col = static_cast<float*>(p.out) + n;
 #pragma unroll
           for (int i = 0; i < CH; ++i)

@@ -107,8 +107,10 @@ def unshuffle_weight_16x16(w: torch.Tensor, stream=None) -> torch.Tensor:
 
 def mxfp8_gemm(a: torch.Tensor, b: torch.Tensor, sfa_tc: torch.Tensor, sfb_tc: torch.Tensor,
                out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16, alpha: float = 1.0,
-               b_preshuffled: bool = False, log2_k_split: int = 0, stream=None) -> torch.Tensor:
-    """D[M, N] = alpha * A[M, K] . B[N, K]^T, MXFP8 operands with tensor-core-layout scales."""
+               b_preshuffled: bool = False, log2_k_split: int = 0, stream=None, c: torch.Tensor | None = None,
+               beta: float = 0.0, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """D[M, N] = alpha * A[M, K] . B[N, K]^T (+ beta * c + bias[n]), MXFP8 operands with
+    tensor-core-layout scales."""
     m, k = a.shape
     n = b.shape[0]
     if out is None:
@@ -116,13 +118,30 @@ def mxfp8_gemm(a: torch.Tensor, b: torch.Tensor, sfa_tc: torch.Tensor, sfb_tc: t
     args = capi.Mxfp8Args(a.data_ptr(), b.data_ptr(), sfa_tc.data_ptr(), sfb_tc.data_ptr(), out.data_ptr(),
                           m, n, k, a.stride(0), k if b_preshuffled else b.stride(0), out.stride(0), alpha,
                           int(b_preshuffled), _out_code(out.dtype), log2_k_split)
-    capi.check(capi.lib().b2g_gemm_mxfp8(C.byref(args), _stream(stream)), "b2g_gemm_mxfp8")
+    epi = _epilogue(c, beta, bias, out)
+    if epi is None:
+        capi.check(capi.lib().b2g_gemm_mxfp8(C.byref(args), _stream(stream)), "b2g_gemm_mxfp8")
+    else:
+        capi.check(capi.lib().b2g_gemm_mxfp8_ex(C.byref(args), C.byref(epi), _stream(stream)), "b2g_gemm_mxfp8_ex")
     return out
+
+
+def _epilogue(c, beta, bias, out):
+    """b2g_epilogue for D = alpha * A . B^T + beta * c + bias[n], or None without terms.
+    c and bias must have the output's dtype (c [M, >= N] rows, bias [N])."""
+    if c is None and bias is None:
+        return None
+    for t, name in ((c, "c"), (bias, "bias")):
+        if t is not None and t.dtype != out.dtype:
+            raise ValueError(f"{name} must have the output dtype {out.dtype}")
+    return capi.Epilogue(c.data_ptr() if c is not None else None, c.stride(0) if c is not None else 0,
+                         float(beta), bias.data_ptr() if bias is not None else None)
 
 
 def mxfp4_gemm(a: torch.Tensor, b: torch.Tensor, sfa_tc: torch.Tensor, sfb_tc: torch.Tensor,
                out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16, alpha: float = 1.0,
-               b_preshuffled: bool = False, log2_k_split: int = 0, stream=None) -> torch.Tensor:
+               b_preshuffled: bool = False, log2_k_split: int = 0, stream=None, c: torch.Tensor | None = None,
+               beta: float = 0.0, bias: torch.Tensor | None = None) -> torch.Tensor:
     """D[M, N] = alpha * A . B^T with MXFP4 operands (b2g_gemm_mxfp4): a [M, K/2] and
     b [N, K/2] uint8 of packed E2M1 (element 2i in the low nibble), scales in the
     tensor-core atom layout for K elements."""
@@ -133,7 +152,11 @@ def mxfp4_gemm(a: torch.Tensor, b: torch.Tensor, sfa_tc: torch.Tensor, sfb_tc: t
     args = capi.Mxfp8Args(a.data_ptr(), b.data_ptr(), sfa_tc.data_ptr(), sfb_tc.data_ptr(), out.data_ptr(),
                           m, n, 2 * kh, 2 * a.stride(0), 2 * kh if b_preshuffled else 2 * b.stride(0),
                           out.stride(0), alpha, int(b_preshuffled), _out_code(out.dtype), log2_k_split)
-    capi.check(capi.lib().b2g_gemm_mxfp4(C.byref(args), _stream(stream)), "b2g_gemm_mxfp4")
+    epi = _epilogue(c, beta, bias, out)
+    if epi is None:
+        capi.check(capi.lib().b2g_gemm_mxfp4(C.byref(args), _stream(stream)), "b2g_gemm_mxfp4")
+    else:
+        capi.check(capi.lib().b2g_gemm_mxfp4_ex(C.byref(args), C.byref(epi), _stream(stream)), "b2g_gemm_mxfp4_ex")
     return out
 
 

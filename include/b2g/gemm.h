@@ -196,11 +196,30 @@ typedef struct b2g_mxfp8_args {
 
 B2G_API int b2g_gemm_mxfp8(const b2g_mxfp8_args* args, void* stream);
 
+/* Extra epilogue terms: D = alpha * A . B^T + beta * C + bias[n], evaluated in fp32
+ * in that order (each step rounded once, the reference CPU GEMM's v = alpha * acc;
+ * v += beta * C, asm_f4gemm/f4gemm_ref.hpp:179-210, then the per-output-column
+ * bias of the split-K reduce, opus_gemm_dist/.../splitk_reduce_gfx950.cuh:49-60),
+ * then one rounding to D's type.  C and the bias have D's element type; C may be
+ * D itself.  Both are applied where D is written: in the GEMM epilogue, or in the
+ * split-K reduce when log2_k_split > 0 (fp32 output then goes through the
+ * workspace as well).  Bases 16-byte aligned, ldc >= N with a 16-byte row pitch. */
+typedef struct b2g_epilogue {
+    const void* c;        /* beta * C input, or NULL */
+    long long ldc;        /* elements between rows of C */
+    float beta;
+    const void* bias;     /* per-column bias [N], or NULL */
+} b2g_epilogue;
+
+/* b2g_gemm_mxfp8 with the terms of *epi (epi may be NULL: no terms). */
+B2G_API int b2g_gemm_mxfp8_ex(const b2g_mxfp8_args* args, const b2g_epilogue* epi, void* stream);
+
 /* Native MXFP4 entry over the same argument block: a, b packed E2M1 (two per byte,
  * element 2i in the low nibble), scales in the tensor-core atom layout for K
  * elements (b2g_sf_tc_bytes(rows, k)).  k, lda and ldb count E2M1 elements (even;
  * a row is ld/2 bytes); K % 256 == 0. */
 B2G_API int b2g_gemm_mxfp4(const b2g_mxfp8_args* args, void* stream);
+B2G_API int b2g_gemm_mxfp4_ex(const b2g_mxfp8_args* args, const b2g_epilogue* epi, void* stream);
 
 /* Column-parallel MXFP8 GEMM for one GPU of a multi-GPU job with the output
  * all-gather folded into the epilogue (no counterpart in the reference, whose

@@ -585,3 +585,46 @@ def test_static_weights_decode_waits_for_activations(dev, oracle):
     finally:
         ops.set_static_weights(False)
     assert ops.device_status() == 0
+
+
+# ------------------------------------------------------------------ fused epilogue terms
+# D = alpha * A . B^T + beta * C + bias[n] (b2g_gemm_mxfp8_ex): the reference CPU GEMM's
+# v = alpha * acc; v += beta * C (f4gemm_ref.hpp:179-210), then the split-K reduce's
+# per-column bias (splitk_reduce_gfx950.cuh:49-60), each in fp32.  Routes: CTA pair
+# (M > 128), decode kernel (M <= 128), split-K through the workspace and the reduce.
+@pytest.mark.parametrize("M,N,K,log2", [(512, 512, 1024, 0), (16, 4096, 1024, 0), (300, 1024, 2048, 2),
+                                        (200, 768, 512, 0)])
+@pytest.mark.parametrize("out", ["bf16", "f32"])
+@pytest.mark.parametrize("in_place", [False, True])
+def test_mxfp8_epilogue_beta_bias(dev, oracle, M, N, K, log2, out, in_place):
+    from gcnasm_b200 import ops
+    od = torch.bfloat16 if out == "bf16" else torch.float32
+    qa, sa, qb, sb = mx_operands(oracle, M, N, K)
+    alpha, beta = 0.5, -0.75
+    acc = oracle.gemm_mx(qa, qb, sa, sb, M, N, K, acc_f64=True)
+    c_in = torch.from_numpy(oracle.normal_rows(77, 0, M, N)).to(od)
+    bias = torch.from_numpy(oracle.normal_rows(78, 0, 1, N)[0] * 4).to(od)
+    v = np.float32(alpha) * acc.astype(np.float32)
+    v = (v + np.float32(beta) * c_in.float().numpy()).astype(np.float32)
+    ref = (v + bias.float().numpy()[None, :]).astype(np.float64)
+    dC = c_in.to(dev)
+    out_t = dC if in_place else torch.full((M, N), float("nan"), dtype=od, device=dev)
+    ops.mxfp8_gemm(T(qa, dev), T(qb, dev), T(oracle.sf_to_tc_layout(sa), dev), T(oracle.sf_to_tc_layout(sb), dev),
+                   out=out_t, alpha=alpha, log2_k_split=log2, c=dC, beta=beta, bias=bias.to(dev))
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    check_out(out_t, ref, od)
+
+
+def test_mxfp8_epilogue_bias_only(dev, oracle):
+    """bias without a C term, bf16 output, ragged M and N"""
+    from gcnasm_b200 import ops
+    M, N, K = 333, 1040, 512
+    qa, sa, qb, sb = mx_operands(oracle, M, N, K)
+    bias = torch.from_numpy(oracle.normal_rows(5, 0, 1, N)[0]).to(torch.bfloat16)
+    ref = (oracle.gemm_mx(qa, qb, sa, sb, M, N, K, acc_f64=True).astype(np.float32)
+           + bias.float().numpy()[None, :]).astype(np.float64)
+    got = ops.mxfp8_gemm(T(qa, dev), T(qb, dev), T(oracle.sf_to_tc_layout(sa), dev),
+                         T(oracle.sf_to_tc_layout(sb), dev), out_dtype=torch.bfloat16, bias=bias.to(dev))
+    torch.cuda.synchronize()
+    check_out(got, ref, torch.bfloat16)

@@ -218,6 +218,20 @@ def test_mxfp4_validation_without_gpu():
     assert b"256" in L.b2g_last_error()
 
 
+def test_epilogue_validation_without_gpu():
+    """b2g_gemm_mxfp8_ex refuses misaligned C / bias before any device work."""
+    L = capi.lib()
+    args = capi.Mxfp8Args(0x10000, 0x20000, 0x30000, 0x40000, 0x50000, 256, 1024, 1024, 1024, 1024, 1024, 1.0, 0,
+                          capi.OUT_BF16, 0)
+    epi = capi.Epilogue(0x60008, 1024, 1.0, None)  # C base not 16-byte aligned
+    assert L.b2g_gemm_mxfp8_ex(C.byref(args), C.byref(epi), None) == capi.B2G_ERR_ALIGNMENT
+    epi = capi.Epilogue(0x60000, 1020, 1.0, None)  # ldc < N
+    assert L.b2g_gemm_mxfp8_ex(C.byref(args), C.byref(epi), None) == capi.B2G_ERR_ALIGNMENT
+    epi = capi.Epilogue(None, 0, 0.0, 0x70004)  # bias base not 16-byte aligned
+    assert L.b2g_gemm_mxfp8_ex(C.byref(args), C.byref(epi), None) == capi.B2G_ERR_ALIGNMENT
+    assert b"bias" in L.b2g_last_error()
+
+
 def test_sf_tc_bytes():
     L = capi.lib()
     assert L.b2g_sf_tc_bytes(8192, 8192) == 64 * 64 * 512

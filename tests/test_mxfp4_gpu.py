@@ -197,3 +197,22 @@ def test_mxfp4_single_cta_path(dev):
                        timeout=600)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "single-cta mx4 ok" in r.stdout
+
+
+@pytest.mark.parametrize("M,log2", [(512, 0), (16, 0), (256, 2)])
+def test_mxfp4_epilogue_beta_bias(dev, oracle, M, log2):
+    """b2g_gemm_mxfp4_ex: D = alpha * A . B^T + beta * C + bias[n], C = D in place."""
+    from gcnasm_b200 import ops
+    N, K = 1024, 2048
+    pa, sa, pb, sb = fp4_operands(oracle, M, N, K)
+    alpha, beta = 0.25, 1.5
+    acc = oracle.gemm_mxfp4(pa, pb, sa, sb, M, N, K, acc_f64=True)
+    c_in = torch.from_numpy(oracle.normal_rows(7, 0, M, N))
+    bias = torch.from_numpy(oracle.normal_rows(8, 0, 1, N)[0])
+    v = (np.float32(alpha) * acc.astype(np.float32) + np.float32(beta) * c_in.numpy()).astype(np.float32)
+    ref = (v + bias.numpy()[None, :]).astype(np.float64)
+    dC = c_in.to(dev)
+    ops.mxfp4_gemm(T(pa, dev), T(pb, dev), T(oracle.sf_to_tc_layout(sa), dev), T(oracle.sf_to_tc_layout(sb), dev),
+                   out=dC, alpha=alpha, log2_k_split=log2, c=dC, beta=beta, bias=bias.to(dev))
+    torch.cuda.synchronize()
+    check_out(dC, ref, torch.float32)
