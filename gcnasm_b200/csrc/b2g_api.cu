@@ -305,6 +305,7 @@ struct Req {
   void* const* peer_c = nullptr;
   int n_peers = 0, peer_self = 0;
   long long peer_ldc = 0, peer_col0 = 0;
+  long long peer_shard = 0;  // all-to-all output (b2g_gemm_mxfp8_a2a_out): columns per peer
   // beta * C and a per-column bias (b2g_epilogue), in the output's element type
   EpiTerms epi = {};
 };
@@ -821,6 +822,8 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
     p.peer_first = r.peer_self;
     p.peer_ldc = r.peer_ldc;
     p.peer_col0 = r.peer_col0;
+    p.peer_shard = r.peer_shard;
+    p.peer_row0 = static_cast<long long>(r.peer_self) * r.M;
   } else if (S == 1) {
     p.out_mode = kOutStore;
   } else if (r.out_f32 && !epi_any(r.epi)) {
@@ -1192,6 +1195,36 @@ int b2g_gemm_mxfp8_peer_out(const b2g_mxfp8_args* g, void* const* peer_d, int n_
   r.peer_self = self;
   r.peer_ldc = ldd_full;
   r.peer_col0 = col_offset;
+  return run_gemm(r);
+}
+
+int b2g_gemm_mxfp8_a2a_out(const b2g_mxfp8_args* g, void* const* peer_d, int n_peers, int self, void* stream) {
+  if (!g || !peer_d) return fail(B2G_ERR_INVALID_ARG, "null args");
+  if (g->out_dtype != B2G_OUT_BF16 && g->out_dtype != B2G_OUT_F32) return fail(B2G_ERR_INVALID_ARG, "bad out_dtype");
+  if (n_peers < 1 || n_peers > kMaxPeers) return fail(B2G_ERR_INVALID_ARG, "n_peers must be 1..%d", kMaxPeers);
+  if (self < 0 || self >= n_peers) return fail(B2G_ERR_INVALID_ARG, "self %d outside 0..%d", self, n_peers - 1);
+  if (g->n <= 0 || g->n % n_peers) return fail(B2G_ERR_INVALID_ARG, "N (%d) must split evenly over %d peers", g->n, n_peers);
+  const long long shard = g->n / n_peers;
+  if (shard % 64) return fail(B2G_ERR_UNSUPPORTED, "columns per peer (%lld) must be a multiple of 64", shard);
+  for (int i = 0; i < n_peers; ++i)
+    if (!peer_d[i] || !aligned16(peer_d[i])) return fail(B2G_ERR_ALIGNMENT, "peer buffer %d null or not 16-byte aligned", i);
+  Req r;
+  r.mode = kModeMX;
+  r.bpre = g->b_preshuffled != 0;
+  r.out_f32 = g->out_dtype == B2G_OUT_F32;
+  r.M = g->m; r.N = g->n; r.K = g->k;
+  r.a = g->a; r.lda = g->lda;
+  r.b = g->b; r.ldb = r.bpre ? g->k : g->ldb;
+  r.c = peer_d[self]; r.ldc = g->n;  // C is written only through the peer windows
+  r.alpha = g->alpha;
+  r.sfa = static_cast<const uint8_t*>(g->sfa);
+  r.sfb = static_cast<const uint8_t*>(g->sfb);
+  r.log2_k_split = 0;
+  r.stream = static_cast<cudaStream_t>(stream);
+  r.peer_c = peer_d;
+  r.n_peers = n_peers;
+  r.peer_self = self;
+  r.peer_shard = shard;
   return run_gemm(r);
 }
 

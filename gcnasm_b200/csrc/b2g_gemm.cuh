@@ -69,6 +69,9 @@ struct GemmParams {
   void* peer_c[kMaxPeers];  // out_mode == kOutPeers
   int n_peers, peer_first;  // peer_first: this GPU's index, where a tile's round of peer stores starts
   long long peer_ldc, peer_col0;
+  // all-to-all (peer_shard > 0): column shard q = n / peer_shard goes to peer q only, row
+  // peer_row0 + m of its [rows][peer_shard] window; else every peer gets every column
+  long long peer_shard, peer_row0;
   float alpha;
   EpiTerms epi;  // beta * C and bias, applied where C is written (kOutStore) or in the split-K reduce
   // MX: UE8M0 scales in the tensor-core atom layout (128 rows x 4 K-blocks per
@@ -134,6 +137,23 @@ __device__ __noinline__ void peer_store_warp(const GemmParams& p, const float (&
       __syncwarp();
       // piece i*32 + lane of the staged 16 x 128 bytes: row (..)/8, 16-byte piece (..)%8;
       // re-read from shared memory per peer so that only one piece is live at a time
+      if (p.peer_shard > 0) {  // all-to-all: these CW columns belong to one peer's shard
+        const int n0 = col0 + c * CW;
+        const int q = static_cast<int>(n0 / p.peer_shard);
+        uint8_t* base = static_cast<uint8_t*>(p.peer_c[q]);
+        const long long c_off = n0 - static_cast<long long>(q) * p.peer_shard;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int idx = i * 32 + lane;
+          const int r = idx >> 3, pc = idx & 7;
+          const int m = row0 + 16 * h + r;
+          if (m < p.M && n0 + pc * EP < p.N) {
+            const uint4 v = reinterpret_cast<const uint4*>(stage + r * 128)[pc];
+            st_global_v4(base + ((p.peer_row0 + m) * p.peer_shard + c_off + pc * EP) * es, v.x, v.y, v.z, v.w);
+          }
+        }
+        continue;
+      }
       for (int t = 0; t < p.n_peers; ++t) {
         int q = first + t;
         if (q >= p.n_peers) q -= p.n_peers;

@@ -184,6 +184,23 @@ def mxfp8_gemm_peer_out(a: torch.Tensor, b: torch.Tensor, sfa_tc: torch.Tensor, 
                "b2g_gemm_mxfp8_peer_out")
 
 
+def mxfp8_gemm_a2a_out(a: torch.Tensor, b: torch.Tensor, sfa_tc: torch.Tensor, sfb_tc: torch.Tensor,
+                       window: torch.Tensor, peer_ptrs, self_index: int, alpha: float = 1.0,
+                       b_preshuffled: bool = False, stream=None) -> None:
+    """C = alpha * A . B^T for this GPU's M rows and all N columns, column shard q stored
+    into peer q's window rows [self_index * M, (self_index + 1) * M) (b2g_gemm_mxfp8_a2a_out).
+    window is this GPU's [n_peers * M, N / n_peers] buffer (its dtype is the output type);
+    peer_ptrs[i] the base address of GPU i's window as mapped in this process."""
+    m, k = a.shape
+    n = b.shape[0]
+    args = capi.Mxfp8Args(a.data_ptr(), b.data_ptr(), sfa_tc.data_ptr(), sfb_tc.data_ptr(), 0,
+                          m, n, k, a.stride(0), k if b_preshuffled else b.stride(0), 0, alpha,
+                          int(b_preshuffled), _out_code(window.dtype), 0)
+    ptrs = (C.c_void_p * len(peer_ptrs))(*[C.c_void_p(int(x)) for x in peer_ptrs])
+    capi.check(capi.lib().b2g_gemm_mxfp8_a2a_out(C.byref(args), ptrs, len(peer_ptrs), self_index, _stream(stream)),
+               "b2g_gemm_mxfp8_a2a_out")
+
+
 def opus_kargs(a, b, c, sfa=None, sfb=None, stride_sfa=0, stride_sfb=0, batch=1,
                stride_sfa_batch=0, stride_sfb_batch=0) -> capi.OpusGemmKargs:
     """Fill opus_gemm_kargs the way the reference hosts do

@@ -92,3 +92,24 @@ def n_sharded_peer_out(qa: torch.Tensor, sfa: torch.Tensor, qb_local: torch.Tens
     ops.mxfp8_gemm_peer_out(qa, qb_local, sfa, sfb_local, c_full, peer_ptrs, rank, col0)
     dist.all_reduce(barrier, group=group)
     return c_full
+
+
+def a2a_window(M: int, N: int, world: int, dtype: torch.dtype, group=None) -> tuple[torch.Tensor, list[int]]:
+    """This rank's all-to-all receive window [world * M, N / world] (rows grouped by
+    source rank) in torch symmetric memory, and every rank's window as mapped into
+    this process (rank order)."""
+    return peer_output(world * M, N // world, dtype, group)
+
+
+def gemm_a2a(qa: torch.Tensor, sfa: torch.Tensor, qb: torch.Tensor, sfb: torch.Tensor, window: torch.Tensor,
+             peer_ptrs: list[int], rank: int, barrier: torch.Tensor, group=None) -> torch.Tensor:
+    """MXFP8 GEMM whose output is all-to-all'd in its epilogue (the opus_gemm_dist
+    GEMM -> A2A step): this rank computes C for its own M rows and all N columns and
+    column shard q lands in rank q's window rows [rank * M, (rank + 1) * M).  The
+    all-reduce of `barrier` orders the ranks before any reads its window.  Returns
+    this rank's window: [world * M, N / world], block s from source rank s."""
+    from . import ops
+
+    ops.mxfp8_gemm_a2a_out(qa, qb, sfa, sfb, window, peer_ptrs, rank)
+    dist.all_reduce(barrier, group=group)
+    return window

@@ -236,6 +236,20 @@ B2G_API int b2g_gemm_mxfp4_ex(const b2g_mxfp8_args* args, const b2g_epilogue* ep
 B2G_API int b2g_gemm_mxfp8_peer_out(const b2g_mxfp8_args* args, void* const* peer_d, int n_peers, int self,
                                     long long ldd_full, long long col_offset, void* stream);
 
+/* MXFP8 GEMM with an all-to-all of its output folded into the epilogue: the
+ * "GEMM -> direct A2A" step of opus_gemm_dist (splitk_reduce_gfx950.cuh:276-369,
+ * which stores C column shard p into peer p's window at [src_rank, M, shard_n]).
+ * This GPU computes C = alpha * A[M,K] . B[N,K]^T for its own M rows and all N
+ * columns; column shard q (N / n_peers columns, a multiple of 64) goes to peer q
+ * only, element (m, n) at peer_d[q] + (self * M + m) * shard_n + (n - q * shard_n)
+ * (elements of out_dtype): every peer's window is [n_peers * M][shard_n], rows
+ * grouped by source GPU.  args->d, args->ldd and args->log2_k_split are not used.
+ * peer_d[i] is GPU i's window as mapped into this process (symmetric memory or
+ * CUDA IPC over NVLink).  Plain stores, no waits on other GPUs: the caller orders
+ * every GPU's call before reading a window (a barrier on the stream). */
+B2G_API int b2g_gemm_mxfp8_a2a_out(const b2g_mxfp8_args* args, void* const* peer_d, int n_peers, int self,
+                                   void* stream);
+
 /* b2g_gemm_mxfp8 for callers that cannot allocate device memory.  No counterpart
  * in the reference (its host programs own every buffer and its kernels need no
  * scratch).  Some hosts hand all of the GPU's memory to their own pool at start-up

@@ -628,3 +628,27 @@ def test_mxfp8_epilogue_bias_only(dev, oracle):
                          T(oracle.sf_to_tc_layout(sb), dev), out_dtype=torch.bfloat16, bias=bias.to(dev))
     torch.cuda.synchronize()
     check_out(got, ref, torch.bfloat16)
+
+
+@pytest.mark.parametrize("M,N,K,out,n_peers,self_index", [(512, 1024, 512, "bf16", 4, 1), (300, 768, 1024, "f32", 3, 2),
+                                                          (100, 512, 256, "bf16", 2, 0)])
+def test_mxfp8_a2a_out_local_peers(dev, oracle, M, N, K, out, n_peers, self_index):
+    """b2g_gemm_mxfp8_a2a_out with every "peer" window a separate buffer on this GPU:
+    column shard q of C lands in window q's rows [self * M, (self + 1) * M) and
+    nothing else in any window is written (the pair, single-CTA and ragged-M routes)."""
+    from gcnasm_b200 import ops
+    od = torch.bfloat16 if out == "bf16" else torch.float32
+    qa, sa, qb, sb = mx_operands(oracle, M, N, K)
+    ref = oracle.gemm_mx(qa, qb, sa, sb, M, N, K, acc_f64=True)
+    shard = N // n_peers
+    wins = [torch.full((n_peers * M, shard), float("nan"), dtype=od, device=dev) for _ in range(n_peers)]
+    ops.mxfp8_gemm_a2a_out(T(qa, dev), T(qb, dev), T(oracle.sf_to_tc_layout(sa), dev),
+                           T(oracle.sf_to_tc_layout(sb), dev), wins[self_index],
+                           [w.data_ptr() for w in wins], self_index)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    for q, w in enumerate(wins):
+        block = w[self_index * M:(self_index + 1) * M]
+        check_out(block, ref[:, q * shard:(q + 1) * shard], od)
+        rest = torch.cat([w[:self_index * M], w[(self_index + 1) * M:]])
+        assert torch.isnan(rest.float()).all()

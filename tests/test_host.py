@@ -232,6 +232,22 @@ def test_epilogue_validation_without_gpu():
     assert b"bias" in L.b2g_last_error()
 
 
+def test_a2a_out_validation_without_gpu():
+    """b2g_gemm_mxfp8_a2a_out refuses uneven or too narrow column shards and bad peer
+    lists before any device work (fake, never dereferenced pointers)."""
+    L = capi.lib()
+    args = capi.Mxfp8Args(0x10000, 0x20000, 0x30000, 0x40000, 0, 512, 1024, 1024, 1024, 1024, 0, 1.0, 0,
+                          capi.OUT_BF16, 0)
+    ptrs = (C.c_void_p * 3)(0x100000, 0x200000, 0x300000)
+    assert L.b2g_gemm_mxfp8_a2a_out(C.byref(args), ptrs, 3, 0, None) == capi.B2G_ERR_INVALID_ARG  # 1024 % 3
+    args.n = 288
+    assert L.b2g_gemm_mxfp8_a2a_out(C.byref(args), ptrs, 3, 0, None) == capi.B2G_ERR_UNSUPPORTED  # 96 % 64
+    args.n = 1152
+    assert L.b2g_gemm_mxfp8_a2a_out(C.byref(args), ptrs, 3, 3, None) == capi.B2G_ERR_INVALID_ARG  # self
+    bad = (C.c_void_p * 3)(0x100000, 0x200008, 0x300000)
+    assert L.b2g_gemm_mxfp8_a2a_out(C.byref(args), bad, 3, 0, None) == capi.B2G_ERR_ALIGNMENT
+
+
 def test_sf_tc_bytes():
     L = capi.lib()
     assert L.b2g_sf_tc_bytes(8192, 8192) == 64 * 64 * 512

@@ -3,7 +3,8 @@ the GEMM epilogue (b2g_gemm_mxfp8_peer_out: every rank's columns are stored
 straight into every rank's full-width C in symmetric memory), and the NCCL
 all-gather form, against the single-GPU GEMM of the full problem on the same
 seeded inputs.  Each element is accumulated the same way in all three, so the
-results must be bit-identical.  Needs two GPUs (skipped otherwise); the ranks are
+results must be bit-identical.  Then the GEMM -> all-to-all epilogue
+(b2g_gemm_mxfp8_a2a_out) against each source rank's single-GPU GEMM.  Needs two GPUs (skipped otherwise); the ranks are
 child processes with a short process-group timeout.
 """
 import os
@@ -64,6 +65,30 @@ def _rank_main(rank: int, world: int, port: int) -> None:
             assert ops.device_status() == 0
             dist.barrier()
             del c_full
+        # GEMM -> all-to-all (b2g_gemm_mxfp8_a2a_out): rank s computes C_s for its own
+        # M rows and all N columns; rank r's window gets column shard r of every C_s
+        M, N, K = 256, 1024, 512
+        dtype = torch.bfloat16
+        cols = N // world
+        win, wptrs = shard.a2a_window(M, N, world, dtype)
+        win.fill_(float("nan"))
+        dist.barrier()
+        g = torch.Generator(device=dev)
+        qb, sfb = ops.quant_mxfp8(torch.randn(N, K, device=dev, generator=g.manual_seed(22)), "tc")
+        refs, mine = [], None
+        for src in range(world):
+            qa_s, sfa_s = ops.quant_mxfp8(torch.randn(M, K, device=dev, generator=g.manual_seed(30 + src)), "tc")
+            refs.append(ops.mxfp8_gemm(qa_s, qb, sfa_s, sfb, out_dtype=dtype))
+            if src == rank:
+                mine = (qa_s, sfa_s)
+        barrier = torch.zeros(1, device=dev)
+        out = shard.gemm_a2a(mine[0], mine[1], qb, sfb, win, wptrs, rank, barrier)
+        torch.cuda.synchronize()
+        for src in range(world):
+            assert torch.equal(out[src * M:(src + 1) * M], refs[src][:, rank * cols:(rank + 1) * cols]), (src, rank)
+        assert ops.device_status() == 0
+        dist.barrier()
+        del win
     finally:
         dist.destroy_process_group()
 
