@@ -35,7 +35,8 @@ EXPORTS = [
     "b2g_gemm_a8w8_blockscale", "b2g_gemm_a8w8", "b2g_gemm_a8w8_preshuffled", "b2g_gemm_mxfp8_f4gemm",
     "b2g_gemm_mxfp4_f4gemm", "b2g_gemm_mxfp8", "b2g_gemm_mxfp4", "b2g_gemm_mxfp8_ex", "b2g_gemm_mxfp4_ex", "b2g_gemm_mxfp8_peer_out", "b2g_gemm_mxfp8_a2a_out", "b2g_set_static_weights", "b2g_gemm_mxfp8_noalloc", "b2g_select", "b2g_manifest_size", "b2g_manifest_entry", "b2g_sf_tc_bytes",
     "b2g_sf_rowmajor_to_tc", "b2g_sf_f4gemm_to_tc", "b2g_shuffle_scale", "b2g_shuffle_weight_16x16",
-    "b2g_unshuffle_weight_16x16", "b2g_quant_mxfp8", "b2g_quant_1x128", "b2g_quant_128x128",
+    "b2g_unshuffle_weight_16x16", "b2g_quant_mxfp8", "b2g_quant_mxfp8_ex", "b2g_quant_mxfp4",
+    "b2g_quant_1x128", "b2g_quant_1x128_ex", "b2g_quant_128x128",
     "b2g_device_status", "b2g_set_wait_timeout_ms", "b2g_debug_force_stall", "b2g_status_string",
     "b2g_last_error", "b2g_version",
 ]
@@ -140,6 +141,9 @@ def lib() -> C.CDLL:
         L.b2g_unshuffle_weight_16x16.argtypes = [vp, vp, ci, ci, vp]
         L.b2g_quant_mxfp8.argtypes = [vp, ci, ci, ll, vp, ll, vp, vp, vp]
         L.b2g_quant_1x128.argtypes = [vp, ci, ci, vp, vp, vp]
+        L.b2g_quant_mxfp8_ex.argtypes = [vp, ci, ci, ci, ll, vp, ll, vp, vp, vp]
+        L.b2g_quant_mxfp4.argtypes = [vp, ci, ci, ci, ll, vp, ll, vp, vp, vp]
+        L.b2g_quant_1x128_ex.argtypes = [vp, ci, ci, ci, vp, vp, vp]
         L.b2g_quant_128x128.argtypes = [vp, ci, ci, vp, vp, vp]
         L.b2g_device_status.argtypes = [pi, ci]
         L.b2g_set_wait_timeout_ms.argtypes = [ci]

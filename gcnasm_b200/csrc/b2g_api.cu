@@ -1416,11 +1416,15 @@ int b2g_unshuffle_weight_16x16(const void* src, void* dst, int n, int kp, void* 
 }
 
 // ------------------------------------------------------------ quantisers
-int b2g_quant_mxfp8(const float* x, int rows, int k, long long ldx, void* q, long long ldq, void* sf_tc,
-                    void* sf_rowmajor, void* stream) {
-  if (!x || !q || rows <= 0 || k <= 0 || k % 32 || ldx < k || ldq < k) return fail(B2G_ERR_INVALID_ARG, "bad arguments");
-  if (!aligned16(x) || ldx % 4 || ldq % 8 || (reinterpret_cast<uintptr_t>(q) & 7))
-    return fail(B2G_ERR_ALIGNMENT, "x must be 16-byte aligned with ldx %% 4 == 0; q 8-byte aligned with ldq %% 8 == 0");
+static int run_quant_mx(const void* x, int x_dtype, bool fp4, int rows, int k, long long ldx, void* q,
+                        long long ldq, void* sf_tc, void* sf_rowmajor, void* stream) {
+  if (x_dtype != B2G_OUT_F32 && x_dtype != B2G_OUT_BF16) return fail(B2G_ERR_INVALID_ARG, "x_dtype must be fp32 or bf16");
+  const long long q_row = fp4 ? k / 2 : k;  // bytes of one quantised row
+  if (!x || !q || rows <= 0 || k <= 0 || k % 32 || ldx < k || ldq < q_row) return fail(B2G_ERR_INVALID_ARG, "bad arguments");
+  const long long xe = x_dtype == B2G_OUT_F32 ? 4 : 8;  // elements per 16 bytes
+  if (!aligned16(x) || ldx % xe || (fp4 ? (ldq % 4 || (reinterpret_cast<uintptr_t>(q) & 3))
+                                        : (ldq % 8 || (reinterpret_cast<uintptr_t>(q) & 7))))
+    return fail(B2G_ERR_ALIGNMENT, "x must be 16-byte aligned with 16-byte rows; q rows aligned to 4 (MXFP4) or 8 bytes");
   DevState* d = nullptr;
   int rc = device_state(&d);
   if (rc) return rc;
@@ -1429,24 +1433,63 @@ int b2g_quant_mxfp8(const float* x, int rows, int k, long long ldx, void* q, lon
     B2G_CUDA(cudaMemsetAsync(sf_tc, 0x7F, static_cast<size_t>(b2g_sf_tc_bytes(rows, k)), st));
   }
   const long long work = static_cast<long long>(rows) * (k / 8);
-  b2g_quant_mx_kernel<<<grid_for(work, 256, d->sms), 256, 0, st>>>(x, rows, k, ldx, static_cast<uint8_t*>(q), ldq,
-                                                                     static_cast<uint8_t*>(sf_tc),
-                                                                     static_cast<uint8_t*>(sf_rowmajor));
+  const int grid = grid_for(work, 256, d->sms);
+  uint8_t* qb = static_cast<uint8_t*>(q);
+  uint8_t* stc = static_cast<uint8_t*>(sf_tc);
+  uint8_t* srm = static_cast<uint8_t*>(sf_rowmajor);
+  if (x_dtype == B2G_OUT_F32) {
+    const float* xf = static_cast<const float*>(x);
+    if (fp4) b2g_quant_mx_kernel<true><<<grid, 256, 0, st>>>(xf, rows, k, ldx, qb, ldq, stc, srm);
+    else b2g_quant_mx_kernel<false><<<grid, 256, 0, st>>>(xf, rows, k, ldx, qb, ldq, stc, srm);
+  } else {
+    const __nv_bfloat16* xh = static_cast<const __nv_bfloat16*>(x);
+    if (fp4) b2g_quant_mx_kernel<true><<<grid, 256, 0, st>>>(xh, rows, k, ldx, qb, ldq, stc, srm);
+    else b2g_quant_mx_kernel<false><<<grid, 256, 0, st>>>(xh, rows, k, ldx, qb, ldq, stc, srm);
+  }
   B2G_CUDA(cudaGetLastError());
   return B2G_OK;
 }
 
-int b2g_quant_1x128(const float* x, int rows, int k, void* q, float* sf, void* stream) {
+int b2g_quant_mxfp8(const float* x, int rows, int k, long long ldx, void* q, long long ldq, void* sf_tc,
+                    void* sf_rowmajor, void* stream) {
+  return run_quant_mx(x, B2G_OUT_F32, false, rows, k, ldx, q, ldq, sf_tc, sf_rowmajor, stream);
+}
+
+int b2g_quant_mxfp8_ex(const void* x, int x_dtype, int rows, int k, long long ldx, void* q, long long ldq,
+                       void* sf_tc, void* sf_rowmajor, void* stream) {
+  return run_quant_mx(x, x_dtype, false, rows, k, ldx, q, ldq, sf_tc, sf_rowmajor, stream);
+}
+
+int b2g_quant_mxfp4(const void* x, int x_dtype, int rows, int k, long long ldx, void* q, long long ldq,
+                    void* sf_tc, void* sf_rowmajor, void* stream) {
+  return run_quant_mx(x, x_dtype, true, rows, k, ldx, q, ldq, sf_tc, sf_rowmajor, stream);
+}
+
+static int run_quant_1x128(const void* x, int x_dtype, int rows, int k, void* q, float* sf, void* stream) {
+  if (x_dtype != B2G_OUT_F32 && x_dtype != B2G_OUT_BF16) return fail(B2G_ERR_INVALID_ARG, "x_dtype must be fp32 or bf16");
   if (!x || !q || !sf || rows <= 0 || k <= 0 || k % 128) return fail(B2G_ERR_INVALID_ARG, "bad arguments");
   if (!aligned16(x) || !aligned16(q)) return fail(B2G_ERR_ALIGNMENT, "x and q must be 16-byte aligned");
   DevState* d = nullptr;
   int rc = device_state(&d);
   if (rc) return rc;
   const long long warps = static_cast<long long>(rows) * (k / 128);
-  b2g_quant_1x128_kernel<<<grid_for(warps * 32, 256, d->sms), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      x, rows, k, static_cast<uint8_t*>(q), sf);
+  const int grid = grid_for(warps * 32, 256, d->sms);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (x_dtype == B2G_OUT_F32)
+    b2g_quant_1x128_kernel<<<grid, 256, 0, st>>>(static_cast<const float*>(x), rows, k, static_cast<uint8_t*>(q), sf);
+  else
+    b2g_quant_1x128_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), rows, k,
+                                                 static_cast<uint8_t*>(q), sf);
   B2G_CUDA(cudaGetLastError());
   return B2G_OK;
+}
+
+int b2g_quant_1x128(const float* x, int rows, int k, void* q, float* sf, void* stream) {
+  return run_quant_1x128(x, B2G_OUT_F32, rows, k, q, sf, stream);
+}
+
+int b2g_quant_1x128_ex(const void* x, int x_dtype, int rows, int k, void* q, float* sf, void* stream) {
+  return run_quant_1x128(x, x_dtype, rows, k, q, sf, stream);
 }
 
 int b2g_quant_128x128(const float* x, int n, int k, void* q, float* sf, void* stream) {

@@ -3,7 +3,8 @@
 //   * scale-factor layout conversion between the reference's f4gemm shuffled
 //     layout, plain row-major UE8M0 and the sm_100 tensor-core atom layout
 //   * the reference's 16x16 B preshuffle (and its inverse) on device
-//   * MXFP8 / 1x128 / 128x128 quantisers (the data recipe of the benchmark configs)
+//   * MXFP8 / MXFP4 / 1x128 / 128x128 quantisers (fp32 or bf16 input for the MX and
+//     1x128 forms; the data recipe of the benchmark configs)
 // All of them are byte/integer work bound by HBM: grid-stride loops, 16-byte
 // accesses where the layout allows, grids sized in multiples of the SM count.
 #pragma once
@@ -160,10 +161,52 @@ __device__ __forceinline__ uint8_t mx_scale_byte(float amax) {
   return static_cast<uint8_t>(b);
 }
 
-// MXFP8: one thread per 8 consecutive elements, 4 threads per 1x32 block.
-// K % 32 == 0.  sf_tc (tc atom layout, may be null) and/or sf_rm (row-major
-// [rows, K/32], may be null) receive the scales.
-__global__ void b2g_quant_mx_kernel(const float* __restrict__ x, int rows, int K, long long ldx,
+// MXFP4 element: round to nearest with ties to the even code onto the e2m1 grid
+// {0, 0.5, 1, 1.5, 2, 3, 4, 6} (the midpoints are exact fp32 values), saturating
+// at 6; sign from the sign bit of x; NaN -> 7 | sign.  Nibble code, bit 3 = sign.
+__device__ __forceinline__ uint32_t f32_to_e2m1(float x) {
+  const uint32_t sign = (__float_as_uint(x) >> 28) & 8u;
+  const float a = fabsf(x);
+  uint32_t c = (a <= 0.25f) ? 0u : (a < 0.75f) ? 1u : (a <= 1.25f) ? 2u : (a < 1.75f) ? 3u
+             : (a <= 2.5f) ? 4u : (a < 3.5f) ? 5u : (a <= 5.0f) ? 6u : 7u;
+  if (a != a) c = 7u;
+  return sign | c;
+}
+
+// smallest e with 2^e * 6 >= amax (the MX scale rule with e2m1's largest value),
+// biased and clamped to [1, 254]; 1 for amax == 0
+__device__ __forceinline__ uint8_t mxfp4_scale_byte(float amax) {
+  if (!(amax > 0.f)) return 1;
+  int ex;
+  const float mant = frexpf(amax, &ex);
+  int b = ((mant <= 0.75f) ? ex - 3 : ex - 2) + 127;
+  b = b < 1 ? 1 : (b > 254 ? 254 : b);
+  return static_cast<uint8_t>(b);
+}
+
+// eight consecutive input elements as fp32 (bf16 widens exactly); 16-byte aligned
+__device__ __forceinline__ void load8_f32(const float* p, float (&v)[8]) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(p + 4));
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void load8_f32(const __nv_bfloat16* p, float (&v)[8]) {
+  const uint4 t = __ldg(reinterpret_cast<const uint4*>(p));
+  const uint32_t w[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    v[2 * j] = __uint_as_float(w[j] << 16);
+    v[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+  }
+}
+
+// MX quantiser (kFp4: MXFP4 packed e2m1, else MXFP8 E4M3): one thread per 8
+// consecutive elements, 4 threads per 1x32 block.  K % 32 == 0.  q: E4M3 bytes
+// [rows][ldq] or packed e2m1 (element 2i in the low nibble) [rows][ldq bytes].
+// sf_tc (tc atom layout, may be null) and/or sf_rm (row-major [rows, K/32], may
+// be null) receive the scales.
+template <bool kFp4, typename In>
+__global__ void b2g_quant_mx_kernel(const In* __restrict__ x, int rows, int K, long long ldx,
                                     uint8_t* __restrict__ q, long long ldq, uint8_t* __restrict__ sf_tc,
                                     uint8_t* __restrict__ sf_rm) {
   const int groups = K / 8;
@@ -177,9 +220,7 @@ __global__ void b2g_quant_mx_kernel(const float* __restrict__ x, int rows, int K
     const int g = live ? static_cast<int>(i - r * groups) : 0;
     float v[8];
     if (live) {
-      const float4 a = __ldg(reinterpret_cast<const float4*>(x + r * ldx + g * 8));
-      const float4 b = __ldg(reinterpret_cast<const float4*>(x + r * ldx + g * 8 + 4));
-      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      load8_f32(x + r * ldx + g * 8, v);
     } else {
 #pragma unroll
       for (int j = 0; j < 8; ++j) v[j] = 0.f;
@@ -190,12 +231,19 @@ __global__ void b2g_quant_mx_kernel(const float* __restrict__ x, int rows, int K
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
     if (!live) continue;
-    const uint8_t e = mx_scale_byte(amax);
+    const uint8_t e = kFp4 ? mxfp4_scale_byte(amax) : mx_scale_byte(amax);
     const float inv = __int_as_float((254 - e) << 23);  // 2^(127 - e), exact
-    uint2 pk;
-    pk.x = f32x4_to_e4m3x4_sat(v[0] * inv, v[1] * inv, v[2] * inv, v[3] * inv);
-    pk.y = f32x4_to_e4m3x4_sat(v[4] * inv, v[5] * inv, v[6] * inv, v[7] * inv);
-    *reinterpret_cast<uint2*>(q + r * ldq + g * 8) = pk;
+    if (kFp4) {
+      uint32_t pk = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) pk |= f32_to_e2m1(v[j] * inv) << (4 * j);
+      *reinterpret_cast<uint32_t*>(q + r * ldq + g * 4) = pk;
+    } else {
+      uint2 pk;
+      pk.x = f32x4_to_e4m3x4_sat(v[0] * inv, v[1] * inv, v[2] * inv, v[3] * inv);
+      pk.y = f32x4_to_e4m3x4_sat(v[4] * inv, v[5] * inv, v[6] * inv, v[7] * inv);
+      *reinterpret_cast<uint2*>(q + r * ldq + g * 8) = pk;
+    }
     if ((g & 3) == 0) {
       const int c = g >> 2;
       if (sf_tc) sf_tc[tc_atom_offset(static_cast<int>(r), c, cb_n)] = e;
@@ -206,7 +254,15 @@ __global__ void b2g_quant_mx_kernel(const float* __restrict__ x, int rows, int K
 
 // 1x128 (fp32 scale = amax/448 per 128 elements of a row): one warp per block;
 // sf laid out [K/128, rows].
-__global__ void b2g_quant_1x128_kernel(const float* __restrict__ x, int rows, int K, uint8_t* __restrict__ q,
+__device__ __forceinline__ float4 load4_f32(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+__device__ __forceinline__ float4 load4_f32(const __nv_bfloat16* p) {
+  const uint2 t = __ldg(reinterpret_cast<const uint2*>(p));
+  return make_float4(__uint_as_float(t.x << 16), __uint_as_float(t.x & 0xFFFF0000u), __uint_as_float(t.y << 16),
+                     __uint_as_float(t.y & 0xFFFF0000u));
+}
+
+template <typename In>
+__global__ void b2g_quant_1x128_kernel(const In* __restrict__ x, int rows, int K, uint8_t* __restrict__ q,
                                        float* __restrict__ sf) {
   const int nb = K / 128;
   const long long total = static_cast<long long>(rows) * nb;
@@ -215,7 +271,7 @@ __global__ void b2g_quant_1x128_kernel(const float* __restrict__ x, int rows, in
        w += (static_cast<long long>(gridDim.x) * blockDim.x) >> 5) {
     const long long r = w / nb;
     const int b = static_cast<int>(w - r * nb);
-    const float4 v = __ldg(reinterpret_cast<const float4*>(x + r * K + b * 128 + lane * 4));
+    const float4 v = load4_f32(x + r * K + b * 128 + lane * 4);
     float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));

@@ -35,25 +35,49 @@ def sf_tc_bytes(rows: int, k: int) -> int:
     return int(capi.lib().b2g_sf_tc_bytes(rows, k))
 
 
+def _x_code(x: torch.Tensor) -> int:
+    if x.dtype == torch.float32:
+        return capi.OUT_F32
+    if x.dtype == torch.bfloat16:
+        return capi.OUT_BF16
+    raise ValueError(f"quantiser input must be fp32 or bf16, not {x.dtype}")
+
+
 def quant_mxfp8(x: torch.Tensor, sf_layout: str = "tc", stream=None):
-    """fp32 [rows, K] -> (q uint8 [rows, K], scales uint8) with scales in the
-    tensor-core atom layout ("tc", flat) or row-major [rows, K/32] ("rowmajor")."""
-    assert x.dtype == torch.float32 and x.is_cuda and x.dim() == 2
+    """fp32 or bf16 [rows, K] -> (q uint8 [rows, K] E4M3, scales uint8) with scales in
+    the tensor-core atom layout ("tc", flat) or row-major [rows, K/32] ("rowmajor")."""
+    assert x.is_cuda and x.dim() == 2
     rows, k = x.shape
     q = torch.empty((rows, k), dtype=torch.uint8, device=x.device)
     sf_tc = torch.empty(sf_tc_bytes(rows, k), dtype=torch.uint8, device=x.device) if sf_layout == "tc" else None
     sf_rm = torch.empty((rows, k // 32), dtype=torch.uint8, device=x.device) if sf_layout == "rowmajor" else None
-    capi.check(capi.lib().b2g_quant_mxfp8(x.data_ptr(), rows, k, x.stride(0), q.data_ptr(), q.stride(0),
-                                          _ptr(sf_tc), _ptr(sf_rm), _stream(stream)), "b2g_quant_mxfp8")
+    capi.check(capi.lib().b2g_quant_mxfp8_ex(x.data_ptr(), _x_code(x), rows, k, x.stride(0), q.data_ptr(),
+                                             q.stride(0), _ptr(sf_tc), _ptr(sf_rm), _stream(stream)),
+               "b2g_quant_mxfp8_ex")
+    return q, (sf_tc if sf_layout == "tc" else sf_rm)
+
+
+def quant_mxfp4(x: torch.Tensor, sf_layout: str = "tc", stream=None):
+    """fp32 or bf16 [rows, K] -> (packed E2M1 uint8 [rows, K/2], scales uint8) with
+    scales as in quant_mxfp8 (b2g_quant_mxfp4: s = 2^ceil(log2(amax/6)) per 1x32)."""
+    assert x.is_cuda and x.dim() == 2
+    rows, k = x.shape
+    q = torch.empty((rows, k // 2), dtype=torch.uint8, device=x.device)
+    sf_tc = torch.empty(sf_tc_bytes(rows, k), dtype=torch.uint8, device=x.device) if sf_layout == "tc" else None
+    sf_rm = torch.empty((rows, k // 32), dtype=torch.uint8, device=x.device) if sf_layout == "rowmajor" else None
+    capi.check(capi.lib().b2g_quant_mxfp4(x.data_ptr(), _x_code(x), rows, k, x.stride(0), q.data_ptr(),
+                                          q.stride(0), _ptr(sf_tc), _ptr(sf_rm), _stream(stream)),
+               "b2g_quant_mxfp4")
     return q, (sf_tc if sf_layout == "tc" else sf_rm)
 
 
 def quant_1x128(x: torch.Tensor, stream=None):
+    """fp32 or bf16 [rows, K] -> (E4M3 q, fp32 scales [K/128, rows], amax/448 per 1x128)."""
     rows, k = x.shape
     q = torch.empty((rows, k), dtype=torch.uint8, device=x.device)
     sf = torch.empty((k // 128, rows), dtype=torch.float32, device=x.device)
-    capi.check(capi.lib().b2g_quant_1x128(x.data_ptr(), rows, k, q.data_ptr(), sf.data_ptr(), _stream(stream)),
-               "b2g_quant_1x128")
+    capi.check(capi.lib().b2g_quant_1x128_ex(x.data_ptr(), _x_code(x), rows, k, q.data_ptr(), sf.data_ptr(),
+                                             _stream(stream)), "b2g_quant_1x128_ex")
     return q, sf
 
 

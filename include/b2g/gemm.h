@@ -297,8 +297,21 @@ B2G_API int b2g_unshuffle_weight_16x16(const void* src, void* dst, int n, int kp
  * b2g_sf_tc_bytes(rows, K) bytes) and/or sf_rowmajor ([rows, K/32]) may be NULL. */
 B2G_API int b2g_quant_mxfp8(const float* x, int rows, int k, long long ldx, void* q, long long ldq, void* sf_tc,
                     void* sf_rowmajor, void* stream);
+/* The quantisers below take their input as fp32 or bf16 (x_dtype B2G_OUT_F32 or
+ * B2G_OUT_BF16: the element type of the activations a caller holds; bf16 widens
+ * to fp32 exactly, so the result is that of the fp32 quantiser on the widened
+ * values).  x 16-byte aligned, ldx a multiple of 8 elements. */
+B2G_API int b2g_quant_mxfp8_ex(const void* x, int x_dtype, int rows, int k, long long ldx, void* q, long long ldq,
+                               void* sf_tc, void* sf_rowmajor, void* stream);
+/* x [rows, K] -> packed E2M1 q [rows, K/2] (element 2i in the low nibble; ldq in
+ * bytes, a multiple of 4) and UE8M0 scales s = 2^ceil(log2(amax/6)) per 1x32 block
+ * (the MXFP8 rule with E2M1's largest value 6), elements rounded to nearest-even
+ * onto the E2M1 grid with saturation.  K % 32 == 0; scale outputs as above. */
+B2G_API int b2g_quant_mxfp4(const void* x, int x_dtype, int rows, int k, long long ldx, void* q, long long ldq,
+                            void* sf_tc, void* sf_rowmajor, void* stream);
 /* 1x128 fp32 scales (amax/448), sf [K/128, rows] */
 B2G_API int b2g_quant_1x128(const float* x, int rows, int k, void* q, float* sf, void* stream);
+B2G_API int b2g_quant_1x128_ex(const void* x, int x_dtype, int rows, int k, void* q, float* sf, void* stream);
 /* 128x128 fp32 scales, sf [N/128, K/128] */
 B2G_API int b2g_quant_128x128(const float* x, int n, int k, void* q, float* sf, void* stream);
 

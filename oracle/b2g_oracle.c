@@ -422,6 +422,66 @@ static const float k_e2m1[16] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f,
 
 ORC_API float orc_e2m1_to_f32(uint8_t nib) { return k_e2m1[nib & 15]; }
 
+/* fp32 -> e2m1 nibble, round to nearest with ties to the even code (codes 0, 2, 4,
+ * 6 have a zero mantissa bit), saturating at 6: the thresholds are the midpoints
+ * of the e2m1 grid {0, 0.5, 1, 1.5, 2, 3, 4, 6}, all exact in fp32.  The sign
+ * bit follows the sign of x (so -0.1 gives -0).  NaN maps to code 7 | sign. */
+ORC_API uint8_t orc_f32_to_e2m1(float x)
+{
+    uint8_t sign = (f32_bits(x) >> 31) ? 8 : 0;
+    float a = fabsf(x);
+    uint8_t c;
+    if (a != a) c = 7;
+    else if (a <= 0.25f) c = 0;
+    else if (a < 0.75f) c = 1;
+    else if (a <= 1.25f) c = 2;
+    else if (a < 1.75f) c = 3;
+    else if (a <= 2.5f) c = 4;
+    else if (a < 3.5f) c = 5;
+    else if (a <= 5.0f) c = 6;
+    else c = 7;
+    return sign | c;
+}
+
+/* MXFP4 block scale: the reference's MX rule s = 2^ceil(log2(amax / max_elem))
+ * (mla_agentic_v0/flash_mla/quant.py:28-37, E4M3's 448) with e2m1's largest value
+ * 6 in its place, so every |x / s| <= 6; biased and clamped to [1, 254]; an
+ * all-zero block gets 1 (2^-126).  The reference ships no MXFP4 quantiser of its
+ * own (aiter's dynamic_mxfp4_quant is not part of it). */
+ORC_API uint8_t orc_mxfp4_scale_byte(float amax)
+{
+    if (!(amax > 0.0f)) return 1;
+    int ex;
+    float mant = frexpf(amax, &ex);        /* amax = mant * 2^ex, mant in [0.5,1) */
+    int e = (mant <= 0.75f) ? ex - 3 : ex - 2; /* 6 = 0.75 * 2^3 */
+    int b = e + 127;
+    if (b < 1) b = 1;
+    if (b > 254) b = 254;
+    return (uint8_t)b;
+}
+
+/* MXFP4 quantiser: x [rows, K] fp32 -> packed e2m1 q [rows, K/2] (element 2i in the
+ * low nibble) and sf [rows, K/32] UE8M0.  K % 32 == 0. */
+ORC_API void orc_quant_mxfp4(const float* x, int64_t rows, int64_t K, uint8_t* q, uint8_t* sf)
+{
+    int64_t nb = K / 32;
+#pragma omp parallel for
+    for (int64_t r = 0; r < rows; ++r) {
+        for (int64_t b = 0; b < nb; ++b) {
+            float amax = 0.0f;
+            for (int64_t k = b * 32; k < b * 32 + 32; ++k) { float a = fabsf(x[r * K + k]); if (a > amax) amax = a; }
+            uint8_t e = orc_mxfp4_scale_byte(amax);
+            sf[r * nb + b] = e;
+            float inv = ldexpf(1.0f, 127 - (int)e); /* exact 1/s */
+            for (int64_t k = b * 32; k < b * 32 + 32; k += 2) {
+                uint8_t lo = orc_f32_to_e2m1(x[r * K + k] * inv);
+                uint8_t hi = orc_f32_to_e2m1(x[r * K + k + 1] * inv);
+                q[r * (K / 2) + k / 2] = (uint8_t)((hi << 4) | lo);
+            }
+        }
+    }
+}
+
 /* MXFP4 reference GEMM, the f4gemm path itself: every element dequantised as
  * e2m1(nibble) * 2^(e-127) (make_operand, f4gemm_ref.hpp:150-177), then
  * D = alpha * A.B^T accumulated in f64 like reference_gemm (f4gemm_ref.hpp:181-222)

@@ -66,6 +66,9 @@ def lib() -> C.CDLL:
         L.orc_gemm_mx.argtypes = [u8p, u8p, u8p, u8p] + [ci] * 7 + [C.c_float, ci, f32p, ci]
         L.orc_gemm_mxfp4.argtypes = [u8p, u8p, u8p, u8p] + [ci] * 7 + [C.c_float, ci, f32p, ci]
         L.orc_e2m1_to_f32.argtypes = [C.c_uint8]; L.orc_e2m1_to_f32.restype = C.c_float
+        L.orc_f32_to_e2m1.argtypes = [C.c_float]; L.orc_f32_to_e2m1.restype = C.c_uint8
+        L.orc_mxfp4_scale_byte.argtypes = [C.c_float]; L.orc_mxfp4_scale_byte.restype = C.c_uint8
+        L.orc_quant_mxfp4.argtypes = [f32p, i64, i64, u8p, u8p]
         L.orc_shuffle_weight_16x16.argtypes = [u8p, u8p, ci, ci]
         L.orc_shuffle_scale.argtypes = [u8p, ci, ci, ci, ci, u8p]
         L.orc_flatmm_shuffle_b.argtypes = [u8p, u8p, ci, ci]
@@ -218,6 +221,17 @@ def gemm_mxfp4(a, b, sfa, sfb, m, n, k, alpha=1.0, acc_f64=True):
 
 E2M1 = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0, -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0],
                 dtype=np.float32)
+
+
+def quant_mxfp4(x: np.ndarray):
+    """fp32 [rows, K] -> (packed e2m1 [rows, K/2], UE8M0 scales [rows, K/32]); the MX
+    scale rule with e2m1's max 6, round to nearest even onto the e2m1 grid."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    rows, K = x.shape
+    q = np.empty((rows, K // 2), dtype=np.uint8)
+    sf = np.empty((rows, K // 32), dtype=np.uint8)
+    lib().orc_quant_mxfp4(x, rows, K, q, sf)
+    return q, sf
 
 
 def e2m1_decode(packed: np.ndarray) -> np.ndarray:

@@ -80,6 +80,63 @@ def test_quant_mx_bitexact(dev, oracle, M, K):
     assert np.array_equal(sf_tc.cpu().numpy(), oracle.sf_to_tc_layout(sf_ref))
 
 
+@pytest.mark.parametrize("M,K", [(300, 512), (129, 4096)])
+def test_quant_bf16_input_bitexact(dev, oracle, M, K):
+    """bf16 activations into the MXFP8 and 1x128 quantisers: bit-identical to the fp32
+    quantiser on the (exactly) widened values."""
+    from gcnasm_b200 import ops
+    xb = torch.from_numpy(oracle.normal_rows(77, 0, M, K) * 5.0).to(torch.bfloat16)
+    xf = xb.float().numpy()
+    q_ref, sf_ref = oracle.quant_mx(xf)
+    q, sf = ops.quant_mxfp8(xb.to(dev), "rowmajor")
+    q1_ref, s1_ref = oracle.quant_1x128(xf)
+    q1, s1 = ops.quant_1x128(xb.to(dev))
+    torch.cuda.synchronize()
+    assert np.array_equal(q.cpu().numpy(), q_ref) and np.array_equal(sf.cpu().numpy(), sf_ref)
+    assert np.array_equal(q1.cpu().numpy(), q1_ref) and np.array_equal(s1.cpu().numpy(), s1_ref)
+
+
+@pytest.mark.parametrize("M,K,dtype", [(300, 512, "f32"), (1, 32, "f32"), (129, 4096, "bf16"), (64, 256, "bf16")])
+def test_quant_mxfp4_bitexact(dev, oracle, M, K, dtype):
+    """b2g_quant_mxfp4 (packed e2m1 + UE8M0 1x32) against the oracle's restatement:
+    packed bytes, row-major scales and the tensor-core scale layout bit-exact; includes
+    an all-zero block, exact e2m1 ties and values past the saturation point."""
+    from gcnasm_b200 import ops
+    x = oracle.normal_rows(4321, 0, M, K) * 3.0
+    x[0, :32] = 0.0
+    if K >= 64:
+        x[0, 32:40] = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, 6.0], np.float32)  # ties, scale 2^0
+        x[0, 40:64] = 0.0
+    t = torch.from_numpy(x)
+    if dtype == "bf16":
+        t = t.to(torch.bfloat16)
+    q_ref, sf_ref = oracle.quant_mxfp4(t.float().numpy())
+    q, sf_tc = ops.quant_mxfp4(t.to(dev), "tc")
+    q2, sf_rm = ops.quant_mxfp4(t.to(dev), "rowmajor")
+    torch.cuda.synchronize()
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+    assert np.array_equal(q2.cpu().numpy(), q_ref)
+    assert np.array_equal(sf_rm.cpu().numpy(), sf_ref)
+    assert np.array_equal(sf_tc.cpu().numpy(), oracle.sf_to_tc_layout(sf_ref))
+
+
+def test_quant_mxfp4_then_gemm(dev, oracle):
+    """bf16 activations and weights quantised on the device to MXFP4, then the MXFP4
+    GEMM: the result is the oracle GEMM of the oracle-quantised operands."""
+    from gcnasm_b200 import ops
+    M, N, K = 256, 512, 1024
+    xb = torch.from_numpy(oracle.normal_rows(5, 0, M, K)).to(torch.bfloat16)
+    wb = torch.from_numpy(oracle.normal_rows(6, 0, N, K)).to(torch.bfloat16)
+    pa, sa = oracle.quant_mxfp4(xb.float().numpy())
+    pb, sb = oracle.quant_mxfp4(wb.float().numpy())
+    ref = oracle.gemm_mxfp4(pa, pb, sa, sb, M, N, K, acc_f64=True)
+    qa, sfa = ops.quant_mxfp4(xb.to(dev))
+    qb, sfb = ops.quant_mxfp4(wb.to(dev))
+    out = ops.mxfp4_gemm(qa, qb, sfa, sfb, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    check_out(out, ref, torch.float32)
+
+
 def test_quant_1x128_and_128x128_bitexact(dev, oracle):
     from gcnasm_b200 import ops
     x = oracle.normal_rows(7, 0, 256, 512)

@@ -136,6 +136,31 @@ def test_mxfp4_oracle_f32_close_to_f64(oracle):
     assert oracle.check_f32(f32, f64) < 1e-5
 
 
+def test_e2m1_rounding_is_nearest_even(oracle):
+    # the MXFP4 quantiser's element rounding against a brute-force search: nearest
+    # value of the e2m1 grid, ties to the even code, saturation at 6, sign kept
+    L = oracle.lib()
+    grid = oracle.E2M1[:8].astype(np.float64)
+    mids = (grid[1:] + grid[:-1]) / 2
+    rs = np.random.RandomState(0)
+    xs = np.concatenate([rs.uniform(-7, 7, 4000), grid, -grid, mids, -mids, [6.5, 100.0, -100.0, -0.1]])
+    for x in xs.astype(np.float32):
+        a = min(abs(float(x)), 6.0)
+        d = np.abs(grid - a)
+        best = np.flatnonzero(d == d.min())
+        code = int(best[0]) if len(best) == 1 else int([b for b in best if b % 2 == 0][0])
+        assert L.orc_f32_to_e2m1(float(x)) == code | (8 if np.signbit(x) else 0), x
+
+
+def test_mxfp4_scale_rule(oracle):
+    # s = 2^ceil(log2(amax / 6)): every |x / s| <= 6, and the next smaller power would overflow
+    L = oracle.lib()
+    for amax in [6.0, 6.0001, 5.999, 3.0, 0.75, 1e-3, 1.0, 12.0, 1e30]:
+        e = L.orc_mxfp4_scale_byte(amax) - 127
+        assert amax / 2.0 ** e <= 6.0 and (e - 1 + 127 < 1 or amax / 2.0 ** (e - 1) > 6.0), amax
+    assert L.orc_mxfp4_scale_byte(0.0) == 1
+
+
 def test_gemm_mx_oracle_consistent(oracle):
     x = oracle.normal_rows(1234, 0, 32, 128)
     w = oracle.normal_rows(5678, 0, 48, 128)
