@@ -352,11 +352,8 @@ int dispatch_pre_out(const Env& d, bool pre, bool f32, const CUtensorMap& ta, co
 template <int kMode>
 int dispatch_bn(const Env& d, int bn, bool pre, bool f32, const CUtensorMap& ta, const CUtensorMap& tb,
                 const GemmParams& p, int grid, cudaStream_t st) {
-  // The blockwise mode runs 128-wide tiles only: it keeps 64 fp32 sums per epilogue
-  // thread at kBN = 128 (128 at kBN = 256, beyond the 168-register budget of a
-  // 10-warp CTA); no 256-wide blockwise kernel is compiled.
-  if constexpr (kMode != kModeBlk)
-    if (bn == 256) return dispatch_pre_out<kMode, 256>(d, pre, f32, ta, tb, p, grid, st);
+  // (the 256-wide blockwise tile runs its 12-warp register split, GemmCfg::kWide)
+  if (bn == 256) return dispatch_pre_out<kMode, 256>(d, pre, f32, ta, tb, p, grid, st);
   if (bn != 128) return fail(B2G_ERR_UNSUPPORTED, "no single-CTA kernel of width %d", bn);
   return dispatch_pre_out<kMode, 128>(d, pre, f32, ta, tb, p, grid, st);
 }
@@ -434,9 +431,24 @@ int maybe_sync_check() {
 }
 
 // Tile width, split count and K-blocks per split for a request.
+// Widest single-CTA tile of the blockwise mode.  With 128x128 weight scales and
+// more than 128 rows the 12-warp 256-wide tile runs 30-43 % faster than the
+// 128-wide one at C3's shapes (M = 1024..16384); at M = 128 (split-K, HBM-bound)
+// the 128-wide tile's four TMEM partial buffers win on two of the three shapes;
+// with per-column weight scales (GROUP_N = 1) the wide tile is slower (833
+// against ~1350 TFLOP/s at 16384x7168x18432: twice the per-column scale staging
+// per K block).  B2G_BLK_BN=128 caps every blockwise GEMM at 128.
+int blk_max_bn(const Req& r) {
+  static const bool cap = [] {
+    const char* v = getenv("B2G_BLK_BN");
+    return v && atoi(v) == 128;
+  }();
+  return (cap || r.group_n == 1 || r.M <= 128) ? 128 : 256;
+}
+
 int plan_tiles(const Req& r, int sms, int* bn_out, int* S_out, int* kb_per_out, int* bm_out = nullptr) {
   int bn = r.bn, l2 = r.log2_k_split, bm = 128;
-  if (r.mode == kModeBlk && bn == 256) bn = 128;
+  if (r.mode == kModeBlk && bn > blk_max_bn(r)) bn = blk_max_bn(r);
   if (bn == 0) {
     // The pair tile wastes half its rows at M <= 128 and the blockwise mode has no
     // pair kernel: those select among the single-CTA entries only.
@@ -446,7 +458,7 @@ int plan_tiles(const Req& r, int sms, int* bn_out, int* S_out, int* kb_per_out, 
     }();
     const bool pair_ok = r.M > 128 && r.mode != kModeBlk && !pair_off;
     int idx = -1, lsel = 0;
-    select_tile(r.M, r.N, sms, r.log2_k_split, r.bpre ? 1 : 0, &idx, &lsel, r.mode == kModeBlk ? 128 : 1 << 30,
+    select_tile(r.M, r.N, sms, r.log2_k_split, r.bpre ? 1 : 0, &idx, &lsel, r.mode == kModeBlk ? blk_max_bn(r) : 1 << 30,
                 pair_ok ? 1 << 30 : 128);
     if (idx < 0) return fail(B2G_ERR_UNSUPPORTED, "no tile in the manifest fits");
     bn = kManifest[idx].tile_n;
@@ -455,7 +467,7 @@ int plan_tiles(const Req& r, int sms, int* bn_out, int* S_out, int* kb_per_out, 
   }
   // the widths the kernels are compiled for: pair 256, single CTA 256 / 128
   if (bm == 256) bn = 256;
-  else bn = (r.mode != kModeBlk && bn == 256) ? 256 : 128;
+  else bn = (bn == 256 && (r.mode != kModeBlk || blk_max_bn(r) == 256)) ? 256 : 128;
   if (bm_out) *bm_out = bm;
   if (l2 < 0) l2 = 0;
   if (l2 > 8) return fail(B2G_ERR_INVALID_ARG, "log2_k_split %d too large", l2);

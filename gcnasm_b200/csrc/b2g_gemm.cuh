@@ -242,7 +242,14 @@ struct GemmCfg {
   static constexpr bool kBPre = kBPre_;     // B given 16x16-preshuffled ([N/16][K/16][16][16] bytes)
   static constexpr bool kOutF32 = kOutF32_;
   static constexpr int kBM = 128, kBK = 128, kUmmaK = 32;
-  static constexpr int kThreads = 320;
+  // The 256-wide blockwise tile keeps 128 fp32 sums per epilogue thread: it runs
+  // 12 warps (warpgroup 0: producer, MMA issuer, two idle warps; warpgroups 1-2:
+  // the 8 epilogue warps) and moves registers from warpgroup 0 (56 each) to the
+  // epilogue (224 each): 128 * 56 + 256 * 224 = 384 * 168, the launch's total.
+  // Every other tile: 10 warps, epilogue warps 2..9.
+  static constexpr bool kWide = kMode == kModeBlk && kBN_ == 256;
+  static constexpr int kThreads = kWide ? 384 : 320;
+  static constexpr int kFirstEpiWarp = kWide ? 4 : 2;
   static constexpr int kEpiWarps = 8;
   static constexpr int kColsPerThread = kBN / 2;  // each epilogue thread: one row, half the tile
   static constexpr int kChunks = kColsPerThread / 32;
@@ -332,8 +339,11 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
   const uint32_t tmem_base = *tmem_holder;
   const uint64_t tmo = p.timeout_ns;
 
+  // kWide: each role's branch opens with its warpgroup's register re-split, so the
+  // compiler allocates the epilogue's code with 224 registers
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
+    if constexpr (Cfg::kWide) setmaxnreg_dec<56>();
     if (lane == 0) {
       tma_prefetch_desc(&tm_a);
       tma_prefetch_desc(&tm_b);
@@ -383,6 +393,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
+    if constexpr (Cfg::kWide) setmaxnreg_dec<56>();
     if (lane == 0) {
       int s = 0, as = 0;
       uint32_t ph = 0, aph = 0, sfbuf = 0;
@@ -452,9 +463,13 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       mbar_wait(fin, 0, &no_abort, p.status, kDevTimeoutDrain, 1000000000ull);
     }
     __syncwarp();
+  } else if (warp < Cfg::kFirstEpiWarp) {
+    // ------------------------------------------------------------ idle (kWide: the rest of warpgroup 0)
+    if constexpr (Cfg::kWide) setmaxnreg_dec<56>();
   } else {
     // ------------------------------------------------------------ epilogue
-    const int ew = warp - 2;
+    if constexpr (Cfg::kWide) setmaxnreg_inc<224>();
+    const int ew = warp - Cfg::kFirstEpiWarp;
     const int quad = warp & 3;                 // TMEM lane group this warp may access
     const int half = ew >> 2;                  // which half of the tile's columns
     const int row_in_tile = quad * 32 + lane;

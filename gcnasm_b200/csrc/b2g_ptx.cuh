@@ -272,6 +272,13 @@ __device__ __forceinline__ void mma_mxf8f6f4(uint32_t d_tmem, uint64_t adesc, ui
       : "memory");
 }
 
+// Register re-split between warpgroups (all four warps of a warpgroup execute
+// the same one): the registers a warpgroup releases go to those that ask for more.
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N)); }
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N)); }
+
 // kind::mxf4.block_scale.scale_vec::2X: packed E2M1 operands, K = 64 per
 // instruction (32 bytes, the same smem footprint as one 32-K E4M3 step), two
 // UE8M0 scales per row per instruction.

@@ -345,6 +345,24 @@ def test_blockscale_splitk(dev, oracle, log2):
         check_out(out, ref, od)
 
 
+# Shapes whose fewest-waves tile is the 256-wide blockwise tile (12 warps, the
+# register re-split between warpgroups): one wave at 256 against two at 128, a
+# ragged M, and a K split; 128x128 weight scales.
+@pytest.mark.parametrize("M,N,K,log2", [(2048, 2048, 512, 0), (1100, 4096, 512, 0), (1024, 4096, 2048, 1)])
+@pytest.mark.parametrize("out_dtype", ["f32", "bf16"])
+def test_blockscale_wide_tile(dev, oracle, M, N, K, log2, out_dtype):
+    from gcnasm_b200 import ops
+    od = torch.bfloat16 if out_dtype == "bf16" else torch.float32
+    qa, sfa = oracle.quant_1x128(oracle.normal_rows(31, 0, M, K))
+    qb, sfb = oracle.quant_128x128(oracle.normal_rows(32, 0, N, K))
+    ref = oracle.gemm_blockscale_f64(qa, qb, sfa, sfb, M, N, K, M, K // 128, 128, 0)
+    out = ops.gemm_a8w8_blockscale(T(qa, dev), T(qb, dev), T(sfa, dev), T(sfb, dev), group_n=128, out_dtype=od,
+                                   log2_k_split=log2)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    check_out(out, ref, od)
+
+
 # ------------------------------------------------------------------ plain fp8 (fp8_gemm / flatmm)
 @pytest.mark.parametrize("M,N,K", [(256, 512, 256), (100, 256, 512)])
 def test_a8w8(dev, oracle, M, N, K):
