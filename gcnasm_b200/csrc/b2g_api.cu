@@ -431,19 +431,20 @@ int maybe_sync_check() {
 }
 
 // Tile width, split count and K-blocks per split for a request.
-// Widest single-CTA tile of the blockwise mode.  With 128x128 weight scales and
-// more than 128 rows the 12-warp 256-wide tile runs 30-43 % faster than the
-// 128-wide one at C3's shapes (M = 1024..16384); at M = 128 (split-K, HBM-bound)
-// the 128-wide tile's four TMEM partial buffers win on two of the three shapes;
-// with per-column weight scales (GROUP_N = 1) the wide tile is slower (833
-// against ~1350 TFLOP/s at 16384x7168x18432: twice the per-column scale staging
-// per K block).  B2G_BLK_BN=128 caps every blockwise GEMM at 128.
+// Widest single-CTA tile of the blockwise mode.  For more than 128 rows the
+// 12-warp 256-wide tile runs 30-43 % faster than the 128-wide one at C3's shapes
+// with 128x128 weight scales (M = 1024..16384) and 23-40 % faster with per-column
+// weight scales (GROUP_N = 1); at M = 128 (split-K, HBM-bound) the 128-wide tile's
+// four TMEM partial buffers win on two of C3's three shapes.  B2G_BLK_BN=128 or
+// 256 sets the width for every blockwise GEMM.
 int blk_max_bn(const Req& r) {
-  static const bool cap = [] {
+  static const int force = [] {
     const char* v = getenv("B2G_BLK_BN");
-    return v && atoi(v) == 128;
+    const int w = v ? atoi(v) : 0;
+    return (w == 128 || w == 256) ? w : 0;
   }();
-  return (cap || r.group_n == 1 || r.M <= 128) ? 128 : 256;
+  if (force) return force;
+  return r.M <= 128 ? 128 : 256;
 }
 
 int plan_tiles(const Req& r, int sms, int* bn_out, int* S_out, int* kb_per_out, int* bm_out = nullptr) {
@@ -468,6 +469,7 @@ int plan_tiles(const Req& r, int sms, int* bn_out, int* S_out, int* kb_per_out, 
   // the widths the kernels are compiled for: pair 256, single CTA 256 / 128
   if (bm == 256) bn = 256;
   else bn = (bn == 256 && (r.mode != kModeBlk || blk_max_bn(r) == 256)) ? 256 : 128;
+  if (r.mode == kModeBlk && bm == 128 && getenv("B2G_BLK_BN")) bn = blk_max_bn(r);  // a forced width
   if (bm_out) *bm_out = bm;
   if (l2 < 0) l2 = 0;
   if (l2 > 8) return fail(B2G_ERR_INVALID_ARG, "log2_k_split %d too large", l2);
