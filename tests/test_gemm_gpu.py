@@ -350,13 +350,18 @@ def test_blockscale_splitk(dev, oracle, log2):
 # ragged M, and a K split; 128x128 weight scales.
 @pytest.mark.parametrize("M,N,K,log2", [(2048, 2048, 512, 0), (1100, 4096, 512, 0), (1024, 4096, 2048, 1)])
 @pytest.mark.parametrize("out_dtype", ["f32", "bf16"])
-def test_blockscale_wide_tile(dev, oracle, M, N, K, log2, out_dtype):
+@pytest.mark.parametrize("group_n", [128, 1])
+def test_blockscale_wide_tile(dev, oracle, M, N, K, log2, out_dtype, group_n):
     from gcnasm_b200 import ops
     od = torch.bfloat16 if out_dtype == "bf16" else torch.float32
     qa, sfa = oracle.quant_1x128(oracle.normal_rows(31, 0, M, K))
-    qb, sfb = oracle.quant_128x128(oracle.normal_rows(32, 0, N, K))
-    ref = oracle.gemm_blockscale_f64(qa, qb, sfa, sfb, M, N, K, M, K // 128, 128, 0)
-    out = ops.gemm_a8w8_blockscale(T(qa, dev), T(qb, dev), T(sfa, dev), T(sfb, dev), group_n=128, out_dtype=od,
+    if group_n == 128:
+        qb, sfb = oracle.quant_128x128(oracle.normal_rows(32, 0, N, K))
+        ref = oracle.gemm_blockscale_f64(qa, qb, sfa, sfb, M, N, K, M, K // 128, 128, 0)
+    else:
+        qb, sfb = oracle.quant_1x128(oracle.normal_rows(32, 0, N, K))  # [K/128, N]
+        ref = oracle.gemm_blockscale_f64(qa, qb, sfa, sfb, M, N, K, M, N, 1, 1)
+    out = ops.gemm_a8w8_blockscale(T(qa, dev), T(qb, dev), T(sfa, dev), T(sfb, dev), group_n=group_n, out_dtype=od,
                                    log2_k_split=log2)
     torch.cuda.synchronize()
     assert ops.device_status() == 0
