@@ -403,6 +403,36 @@ def test_a8w8_batched(dev, oracle):
         check_out(out[b], ref, torch.float32)
 
 
+@pytest.mark.parametrize("group_n", [128, 1])
+def test_blockscale_batched_wide_tile(dev, oracle, group_n):
+    """opus_gemm_kargs with batch = 2 (per-batch A, B, C and scale strides) on a shape
+    whose fewest-waves tile is the 256-wide blockwise tile (2 x 9 x 16 tiles: two waves,
+    against four at 128 wide), both weight-scale layouts, fp32 C."""
+    from gcnasm_b200 import capi, ops
+    Bt, M, N, K = 2, 1100, 4096, 256
+    qas, sas, qbs, sbs, refs = [], [], [], [], []
+    for b in range(Bt):
+        qa, sa = oracle.quant_1x128(oracle.normal_rows(40 + b, 0, M, K))  # sa [K/128, M]
+        if group_n == 128:
+            qb, sb = oracle.quant_128x128(oracle.normal_rows(50 + b, 0, N, K))  # [N/128, K/128]
+            refs.append(oracle.gemm_blockscale_f64(qa, qb, sa, sb, M, N, K, M, K // 128, 128, 0))
+        else:
+            qb, sb = oracle.quant_1x128(oracle.normal_rows(50 + b, 0, N, K))  # [K/128, N]
+            refs.append(oracle.gemm_blockscale_f64(qa, qb, sa, sb, M, N, K, M, N, 1, 1))
+        qas.append(qa); sas.append(sa); qbs.append(qb); sbs.append(sb)
+    a, b_ = T(np.stack(qas), dev), T(np.stack(qbs), dev)
+    sfa, sfb = T(np.stack(sas), dev), T(np.stack(sbs), dev)
+    out = torch.full((Bt, M, N), float("nan"), dtype=torch.float32, device=dev)
+    stride_sfb = K // 128 if group_n == 128 else N
+    ka = ops.opus_kargs(a, b_, out, sfa[0], sfb[0], stride_sfa=M, stride_sfb=stride_sfb, batch=Bt,
+                        stride_sfa_batch=sfa.stride(0), stride_sfb_batch=sfb.stride(0))
+    capi.check(capi.lib().b2g_gemm_a8w8_blockscale(C.byref(ka), group_n, capi.OUT_F32, 0, None), "blockscale")
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    for b in range(Bt):
+        check_out(out[b], refs[b], torch.float32)
+
+
 # ------------------------------------------------------------------ full-size property check
 def test_mxfp8_8192_sampled_rows(dev, oracle):
     """The headline 8192^3 MXFP8 GEMM on the GPU; 64 sampled rows recomputed by the oracle."""
