@@ -362,19 +362,16 @@ def bench_c5(args, dev, stream, world, rank, flush):
     return res
 
 
-def bench_decode(args, dev, stream, peaks, flush):
-    """M=16, N=28672, K=4096 MXFP8, fp32 out (C4): HBM GB/s of the decode GEMM.
-
-    A decode step streams a different weight matrix per GEMM, so B rotates over
-    four copies (4 x 117 MB, well past the 126 MB L2) and the calls run back to
-    back from a CUDA graph, as a decode loop replays them; each replay is
-    bracketed by CUDA events, with a 256 MiB L2 flush before it."""
+def decode_graph_ms(args, dev, stream, flush, M, N, K, static_weights=False):
+    """Milliseconds per call of an MXFP8 decode GEMM (fp32 out) replayed from a
+    CUDA graph: 16 calls back to back with B rotating over enough copies to
+    exceed twice the 126 MB L2, as a decode loop streams a different weight
+    matrix per GEMM; each replay bracketed by CUDA events, L2 flushed before it."""
     import torch
 
     from gcnasm_b200 import ops
 
-    M, N, K = 16, 28672, 4096
-    copies, per_graph = 4, 16
+    copies, per_graph = max(4, -(-2 * (126 << 20) // (N * K))), 16
     qa, sfa_rm, qb, sfb_rm = make_mx_operands(M, N, K, dev, 77)
     sfa, sfb = ops.sf_rowmajor_to_tc(sfa_rm, K), ops.sf_rowmajor_to_tc(sfb_rm, K)
     bs = [qb] + [qb.clone() for _ in range(copies - 1)]
@@ -387,33 +384,48 @@ def bench_decode(args, dev, stream, peaks, flush):
     for i in range(args.warmup * copies):  # module load, scratch, shared-memory attributes
         call(i, stream)
     torch.cuda.synchronize()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
-        for i in range(per_graph):
-            call(i)  # the capture stream
-    g.replay()
-    torch.cuda.synchronize()
-    reps = max(args.steps // 4, 5)
-    times = timed_steps(g.replay, reps, 1, flush, stream)
-    ms = statistics.mean(times) / per_graph
-    del g
-    # the same graph with static weights (b2g_set_static_weights): each call's first
-    # weight loads overlap the tail of the call before it
-    ops.set_static_weights(True)
+    ops.set_static_weights(static_weights)
     try:
-        gs = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(gs):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
             for i in range(per_graph):
-                call(i)
-        gs.replay()
+                call(i)  # the capture stream
+        g.replay()
         torch.cuda.synchronize()
-        ms_s = statistics.mean(timed_steps(gs.replay, reps, 1, flush, stream)) / per_graph
-        del gs
+        reps = max(args.steps // 4, 5)
+        ms = statistics.mean(timed_steps(g.replay, reps, 1, flush, stream)) / per_graph
+        del g
     finally:
         ops.set_static_weights(False)
-    nbytes = M * K + N * K + M * K // 32 + N * K // 32 + 4 * M * N
+    return ms, copies, per_graph, reps
+
+
+def decode_bytes(M, N, K):
+    """Algorithmic bytes of an MXFP8 decode GEMM with fp32 C: A, B, their 1x32
+    scales, C."""
+    return M * K + N * K + M * K // 32 + N * K // 32 + 4 * M * N
+
+
+def bench_decode(args, dev, stream, peaks, flush):
+    """M=16, N=28672, K=4096 MXFP8, fp32 out (C4): HBM GB/s of the decode GEMM,
+    then every C4 shape (M in {1, 16, 64}, (N, K) in {(28672, 4096), (4096, 14336)})
+    by the same method."""
+    M, N, K = 16, 28672, 4096
+    ms, copies, per_graph, reps = decode_graph_ms(args, dev, stream, flush, M, N, K)
+    # the same graph with static weights (b2g_set_static_weights): each call's first
+    # weight loads overlap the tail of the call before it
+    ms_s = decode_graph_ms(args, dev, stream, flush, M, N, K, static_weights=True)[0]
+    nbytes = decode_bytes(M, N, K)
     gbs = nbytes / (ms * 1e-3) / 1e9
     traffic = load_traffic().get("mxfp8_decode_m16_bytes")
+    shapes = []
+    for n, k in ((28672, 4096), (4096, 14336)):
+        for m in (1, 16, 64):
+            t = decode_graph_ms(args, dev, stream, flush, m, n, k)[0]
+            b = decode_bytes(m, n, k)
+            shapes.append({"M": m, "N": n, "K": k, "us_per_call": round(t * 1e3, 2), "algorithmic_bytes": b,
+                           "hbm_gbs": round(b / (t * 1e-3) / 1e9, 1),
+                           "frac": round(b / (t * 1e-3) / 1e9 / peaks["hbm_gbs"], 4)})
     return {"M": M, "N": N, "K": K, "out": "fp32", "us_per_call": round(ms * 1e3, 2),
             "hbm_gbs": round(gbs, 1), "unit": "GB/s", "algorithmic_bytes": nbytes,
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -426,7 +438,8 @@ def bench_decode(args, dev, stream, peaks, flush):
                                "hbm_gbs": round(nbytes / (ms_s * 1e-3) / 1e9, 1),
                                "frac": round(nbytes / (ms_s * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
                                "note": "b2g_set_static_weights(1): B and its scales may be read before the "
-                                       "preceding call completes (serving loop with fixed weights)"}}
+                                       "preceding call completes (serving loop with fixed weights)"},
+            "c4_shapes": shapes}
 
 
 def bench_mxfp4(args, dev, stream, peaks, flush):

@@ -356,6 +356,11 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     // slot and counts in with a CAS; the arrival that completes the count adds.
     constexpr int CH = MP < 32 ? MP : 32;
     constexpr bool kPreload = MP <= 32;  // others' pieces fit in registers ahead of the accumulator
+    // Pieces read from L2 per fold step: their loads are all issued before the
+    // first add, so a tile split over n CTAs costs about n / FB L2 round trips
+    // instead of n.  Two is the most that compiles without spills (MP = 32 keeps
+    // a 32-row preloaded suffix live as well and stays at one).
+    constexpr int FB = MP == 32 ? 1 : 2;
     const int quad = warp & 3;
     const int r = quad * 32 + lane;  // TMEM lane = weight row in the tile = output column in the tile
     const int et = threadIdx.x - 64;
@@ -376,8 +381,55 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       const bool fin_seg = in_sk && q + len == nsk;  // this CTA's last stream-K piece
       unsigned long long* cnt = p.cnt + nt;
       const unsigned long long all_others = (p.tag << 16) | static_cast<unsigned long long>(nseg - 1);
+      // Piece jj's slot.  Only the first owner's range can start before the tile;
+      // every later owner's starts inside it (c0 is the last CTA starting at or
+      // before t0), so its slot is 2 * (c0 + jj): no division per piece.
+      const int slot0 = nseg > 1 ? skinny_slot(c0, nt, U, G, p.KG) : 0;
       auto piece = [&](int jj) {  // this thread's column of piece jj's slot
-        return p.part + static_cast<long long>(skinny_slot(c0 + jj, nt, U, G, p.KG)) * MP * 128 + r;
+        return p.part + static_cast<long long>(jj == 0 ? slot0 : 2 * (c0 + jj)) * MP * 128 + r;
+      };
+
+      const uint32_t acc_addr = tmem_base + lane_addr + as * Cfg::kAccStride;
+      auto load_chunk = [&](int mc, uint32_t (&x)[CH]) {
+        if (CH == 32)
+          tmem_ld_32x32b_x32(acc_addr + mc, *reinterpret_cast<uint32_t(*)[32]>(&x[0]));
+        else
+          tmem_ld_32x32b_x16(acc_addr + mc, *reinterpret_cast<uint32_t(*)[16]>(&x[0]));
+        tc_wait_ld();
+      };
+      // Right fold of the other CTAs' pieces jj = hi .. lo (descending, all != j)
+      // into t, rows [mc, mc + CH); t holds the fold above hi if have_t.  FB
+      // pieces' loads are in flight together; they are still added one at a time
+      // in descending order.
+      auto fold_l2 = [&](int mc, int hi, int lo, float (&t)[CH], bool have_t) {
+#pragma unroll 1
+        for (int jb = hi; jb >= lo; jb -= FB) {
+          float y[FB][CH];
+#pragma unroll
+          for (int b = 0; b < FB; ++b)
+            if (jb - b >= lo) {
+              const float* pj = piece(jb - b) + mc * 128;
+#pragma unroll
+              for (int i = 0; i < CH; ++i) y[b][i] = __ldcg(pj + i * 128);
+            }
+#pragma unroll
+          for (int b = 0; b < FB; ++b)
+            if (jb - b >= lo) {
+#pragma unroll
+              for (int i = 0; i < CH; ++i) t[i] = have_t ? y[b][i] + t[i] : y[b][i];
+              have_t = true;
+            }
+        }
+        return have_t;
+      };
+      // the whole right fold p_0 + (p_1 + (... + p_{n-1})) over pieces j .. 0 (this
+      // CTA's piece j from TMEM) into t, which holds the fold above j if have_t
+      auto fold = [&](int mc, float (&t)[CH], bool have_t) {
+        uint32_t v[CH];
+        load_chunk(mc, v);
+#pragma unroll
+        for (int i = 0; i < CH; ++i) t[i] = have_t ? __uint_as_float(v[i]) + t[i] : __uint_as_float(v[i]);
+        fold_l2(mc, j - 1, 0, t, true);
       };
 
       // This CTA's last piece of a split tile usually finishes after the tile's
@@ -390,23 +442,12 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         if (et == 0) *last_flag = ld_acquire_gpu_u64(cnt) == all_others ? 1u : 0u;
         skinny_epi_bar();
         last = *last_flag != 0;
-        if (kPreload && last) {
-          for (int jj = nseg - 1; jj > j; --jj) {
-            const float* pj = piece(jj);
-            float y[CH];
-#pragma unroll
-            for (int i = 0; i < CH; ++i) y[i] = __ldcg(pj + i * 128);
-#pragma unroll
-            for (int i = 0; i < CH; ++i) suffix[i] = have_suffix ? y[i] + suffix[i] : y[i];
-            have_suffix = true;
-          }
-        }
+        if (kPreload && last && j + 1 < nseg) have_suffix = fold_l2(0, nseg - 1, j + 1, suffix, false);
       }
 
       const bool got = mbar_wait(&acc_full[as], aph, abort_flag, p.status, kDevTimeoutEpilogue, tmo);
       if (!skinny_epi_all(got)) break;
       tc_fence_after();
-      const uint32_t acc_addr = tmem_base + lane_addr + as * Cfg::kAccStride;
       const int n = nt * 128 + r;
       const bool col_ok = n < p.N;
 
@@ -433,34 +474,6 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             if (mc + i < p.M) col[(mc + i) * p.ldo] = __float2bfloat16_rn(x[i] * p.alpha);
         }
       };
-      auto load_chunk = [&](int mc, uint32_t (&x)[CH]) {
-        if (CH == 32)
-          tmem_ld_32x32b_x32(acc_addr + mc, *reinterpret_cast<uint32_t(*)[32]>(&x[0]));
-        else
-          tmem_ld_32x32b_x16(acc_addr + mc, *reinterpret_cast<uint32_t(*)[16]>(&x[0]));
-        tc_wait_ld();
-      };
-      // the right fold over pieces jj = hi .. 0 into t (rows [mc, mc + CH)), this
-      // CTA's piece taken from TMEM; t already holds the fold above hi if have_t
-      auto fold = [&](int mc, int hi, float (&t)[CH], bool have_t) {
-        for (int jj = hi; jj >= 0; --jj) {
-          float y[CH];
-          if (jj == j) {
-            uint32_t v[CH];
-            load_chunk(mc, v);
-#pragma unroll
-            for (int i = 0; i < CH; ++i) y[i] = __uint_as_float(v[i]);
-          } else {
-            const float* pj = piece(jj) + mc * 128;
-#pragma unroll
-            for (int i = 0; i < CH; ++i) y[i] = __ldcg(pj + i * 128);
-          }
-#pragma unroll
-          for (int i = 0; i < CH; ++i) t[i] = have_t ? y[i] + t[i] : y[i];
-          have_t = true;
-        }
-      };
-
       if (nseg == 1) {
 #pragma unroll 1
         for (int mc = 0; mc < MP; mc += CH) {
@@ -510,9 +523,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             if (kPreload && have_suffix) {
 #pragma unroll
               for (int i = 0; i < CH; ++i) t[i] = suffix[i];
-              fold(mc, j, t, true);
+              fold(mc, t, true);
             } else {
-              fold(mc, kPreload && fin_seg ? (have_suffix ? j : nseg - 1) : nseg - 1, t, false);
+              fold(mc, t, fold_l2(mc, nseg - 1, j + 1, t, false));
             }
             store_out(mc, t);
           }

@@ -554,6 +554,27 @@ def test_skinny_decode_shapes(dev, oracle, M, bpre):
     check_out(out, ref, torch.float32)
 
 
+@pytest.mark.parametrize("M", [1, 16, 64])
+@pytest.mark.parametrize("bpre", [False, True])
+def test_skinny_decode_shapes_long_k(dev, oracle, M, bpre):
+    """The second C4 decode shape (N=4096, K=14336), fp32 C: 32 weight tiles for
+    148 CTAs, so every tile's 56 K units are split over about five CTAs and no CTA
+    owns a whole tile."""
+    from gcnasm_b200 import ops
+    N, K = 4096, 14336
+    qa, sa, qb, sb = mx_operands(oracle, M, N, K)
+    ref = oracle.gemm_mx(qa, qb, sa, sb, M, N, K, acc_f64=True)
+    b = T(oracle.shuffle_weight_16x16(qb, N, K).reshape(N, K), dev) if bpre else T(qb, dev)
+    args = (T(qa, dev), b, T(oracle.sf_to_tc_layout(sa), dev), T(oracle.sf_to_tc_layout(sb), dev))
+    out = ops.mxfp8_gemm(*args, out_dtype=torch.float32, b_preshuffled=bpre)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    check_out(out, ref, torch.float32)
+    again = ops.mxfp8_gemm(*args, out_dtype=torch.float32, b_preshuffled=bpre)
+    torch.cuda.synchronize()
+    assert torch.equal(out, again)  # the split-tile partials are folded in a fixed order
+
+
 # Split-tile fixup of the skinny kernel: a tile's K range shared by several CTAs
 # (up to 64 segments when N is small and K large), K not a multiple of 256 (one
 # K block per ring stage) or of 128 (plain (K, rows) maps with a zero-filled
