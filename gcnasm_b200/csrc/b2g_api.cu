@@ -518,12 +518,46 @@ bool use_pdl() {
 
 int skinny_mp(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128; }
 
+
 // 128-K blocks per ring stage: two (one 32 KB request of B) when K splits into
 // whole pairs of blocks and the stage still leaves room for a deep ring.
 int skinny_kkb(const Req& r) { return (r.K % 256 == 0 && skinny_mp(r.M) <= 64) ? 2 : 1; }
 
 long long skinny_units(const Req& r) {
   return static_cast<long long>(cdiv(r.N, 128)) * (cdiv(r.K, 128) / skinny_kkb(r));
+}
+
+// Whole tiles per CTA of a decode launch on G CTAs: NT / G, one less when the
+// leftover tiles would give each CTA under half a tile of stream-K work (many
+// pieces per tile).  The blockwise kernel splits every tile stream-K.
+int skinny_dp_w(const Req& r, int NT, int G) {
+  int dp_w = r.mode == kModeBlk ? 0 : NT / G;
+  if (dp_w > 0 && 2 * (NT - dp_w * G) < G) --dp_w;
+  return dp_w;
+}
+
+// CTAs of a decode launch.  Measured on B200 with two 128-K blocks per stage
+// (M <= 64) and at least 8 stages per tile (the C4 decode shapes, 16 x 57344 x
+// 8192, 16 x 16384 x 3584): a grid whose stream-K units split evenly (every CTA
+// the same number of units, tiles cut into fewer pieces) beats one CTA per SM with
+// uneven shares by 2-17 %, down to about 0.85 x the SM count.  Where a CTA's
+// work is dominated by per-tile costs instead (M = 128: one K block per stage and
+// a 64 KB output tile; K = 1024: four stages per tile) the extra tiles per CTA
+// cost 3-15 %, and the blockwise kernel was not measured: those keep one CTA per
+// SM.  So: the largest even-split grid in [0.85 * sms, sms] when it applies, else
+// sms.  B2G_SKINNY_GRID=<n> forces n CTAs (tuning).
+int skinny_grid(const Req& r, int sms, int NT, int KG) {
+  static const int forced = [] {
+    const char* v = getenv("B2G_SKINNY_GRID");
+    return v ? atoi(v) : 0;
+  }();
+  const long long units = static_cast<long long>(NT) * KG;
+  if (units <= sms) return static_cast<int>(units);
+  if (forced > 0) return std::min(forced, sms);
+  if (r.mode == kModeBlk || skinny_kkb(r) != 2 || KG < 8) return sms;
+  for (int G = sms; 20 * G >= 17 * sms; --G)
+    if ((static_cast<long long>(NT - skinny_dp_w(r, NT, G) * G) * KG) % G == 0) return G;
+  return sms;
 }
 
 // Scratch bytes run_gemm will ask for beyond r.ws_offset.
@@ -635,13 +669,10 @@ int run_skinny(const Req& r, const Env& d) {
   sp.NT = cdiv(r.N, 128);
   sp.KG = cdiv(r.K, 128) / kkb;
   sp.kview = r.K % 128 == 0 ? 1 : 0;
-  const int grid = static_cast<int>(std::min<long long>(skinny_units(r), d.sms));
+  const int grid = skinny_grid(r, d.sms, sp.NT, sp.KG);
   // Whole tiles per CTA, worked after the stream-K units so that every split
-  // tile's fix-up overlaps streaming; one less when the leftover tiles would
-  // give each CTA under half a tile of stream-K work (many pieces per tile).
-  // The blockwise kernel splits every tile stream-K.
-  int dp_w = r.mode == kModeBlk ? 0 : sp.NT / grid;
-  if (dp_w > 0 && 2 * (sp.NT - dp_w * grid) < grid) --dp_w;
+  // tile's fix-up overlaps streaming.
+  const int dp_w = skinny_dp_w(r, sp.NT, grid);
   sp.dp_w = dp_w;
   sp.sk_tiles = sp.NT - dp_w * grid;
   sp.units = static_cast<long long>(sp.sk_tiles) * sp.KG;

@@ -581,7 +581,7 @@ def test_skinny_decode_shapes_long_k(dev, oracle, M, bpre):
 # tail), every padded M, both output types.  The last two have more tiles than
 # 1.5 CTAs' worth: every CTA also owns whole tiles after its stream-K units (two
 # each for N = 449 tiles with a ragged K; one for 297 tiles, where a second would
-# leave one stream-K tile spread over all CTAs).
+# leave each CTA under half a tile of stream-K work).
 SKINNY_SPLIT = [(16, 256, 16384, "f32"), (5, 384, 8320, "bf16"), (16, 512, 4000, "f32"),
                 (64, 1024, 8192, "bf16"), (128, 640, 4096, "f32"), (33, 4096, 2048, "bf16"),
                 (7, 57472, 1056, "bf16"), (20, 38016, 2048, "f32")]
