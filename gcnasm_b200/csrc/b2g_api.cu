@@ -33,6 +33,11 @@ using namespace b2g;
 static constexpr int kSkinnyMaxTiles = 8192;  // N <= 1M
 static __device__ unsigned long long g_skinny_tile_cnt[kSkinnyMaxTiles];
 
+// Status word of the allocating entry points' kernels: zero at load, set (once,
+// by compare-and-swap) by a bounded wait that gives up, read and cleared by
+// b2g_device_status.  A file-scope word, so that reading it allocates nothing.
+static __device__ int g_status_word;
+
 namespace {
 
 constexpr int kVersion = 100;  // 0.1.0
@@ -133,8 +138,11 @@ int device_state(DevState** out, int* dev_out = nullptr) {
     B2G_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
     if (major != 10) return fail(B2G_ERR_NO_DEVICE, "device %d is sm_%d0; this library targets sm_100a", dev, major);
     B2G_CUDA(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev));
-    B2G_CUDA(cudaMalloc(&d.status, sizeof(int)));
-    B2G_CUDA(cudaMemset(d.status, 0, sizeof(int)));
+    void* sw = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress(&sw, g_status_word);
+    if (err != cudaSuccess || !sw)
+      return fail(B2G_ERR_CUDA, "cudaGetSymbolAddress(status word) failed: %s", cudaGetErrorString(err));
+    d.status = static_cast<int*>(sw);
     int rc = skinny_counters(&d.tile_cnt);
     if (rc) return rc;
     d.init = true;
@@ -417,17 +425,24 @@ int dispatch_pair(const Env& d, int mode, int bn, bool pre, bool f32, const CUte
              : launch_pair<PairCfg<kModePlain, 256, false, false>>(d, ta, tb, tsa, tsb, pp, st);
 }
 
-int maybe_sync_check() {
+// B2G_SYNC_CHECK=1: wait for the call's kernels and report (and clear) the
+// status word of the environment they ran in -- the allocating path's word or
+// the no-alloc array's.  A nonzero word also zeroes the decode kernel's tile
+// counters, which a launch that stopped early can leave mid-count.  Allocates
+// nothing.
+int maybe_sync_check(const Env& e) {
   static const bool on = [] {
-    const char* e = getenv("B2G_SYNC_CHECK");
-    return e && e[0] == '1';
+    const char* v = getenv("B2G_SYNC_CHECK");
+    return v && v[0] == '1';
   }();
   if (!on) return B2G_OK;
   int st = 0;
-  int rc = b2g_device_status(&st, 1);
-  if (rc) return rc;
-  if (st) return fail(B2G_ERR_DEVICE_TIMEOUT, "kernel reported device status %d", st);
-  return B2G_OK;
+  B2G_CUDA(cudaDeviceSynchronize());
+  B2G_CUDA(cudaMemcpy(&st, e.status, sizeof(int), cudaMemcpyDeviceToHost));
+  if (!st) return B2G_OK;
+  B2G_CUDA(cudaMemset(e.status, 0, sizeof(int)));
+  B2G_CUDA(cudaMemset(e.tile_cnt, 0, sizeof(unsigned long long) * kSkinnyMaxTiles));
+  return fail(B2G_ERR_DEVICE_TIMEOUT, "kernel reported device status %d", st);
 }
 
 // Tile width, split count and K-blocks per split for a request.
@@ -767,7 +782,7 @@ int run_skinny(const Req& r, const Env& d) {
     rc = r.bpre ? dispatch_skinny_mp<kModePlain, true>(d, mp, kkb, tw, ta, sp, grid, r.stream)
                 : dispatch_skinny_mp<kModePlain, false>(d, mp, kkb, tw, ta, sp, grid, r.stream);
   if (rc) return rc;
-  return maybe_sync_check();
+  return maybe_sync_check(d);
 }
 
 int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
@@ -978,7 +993,7 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
                                                                 r.epi);
     B2G_CUDA(cudaGetLastError());
   }
-  return maybe_sync_check();
+  return maybe_sync_check(d);
 }
 
 }  // namespace
@@ -986,8 +1001,12 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
 // =================================================================== fixed scratch
 // Device scratch for b2g_gemm_mxfp8_noalloc: a file-scope array every GPU that
 // loads this library holds until the process exits.  Bytes [0, 256) hold the
-// kernel status word; the split-K fp32 partials follow.
-static constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;  // 16 MiB
+// kernel status word (zero at load, sticky until b2g_device_status clears it);
+// the rest holds either the split-K fp32 partials (M > 128, bf16 output or a
+// split with fp32 output and epilogue terms) or the decode kernel's fp32 piece
+// slots (M <= 128: 2 * grid * MP * 128 * 4 bytes, 18.5 MiB at M = 128 on 148
+// SMs).  32 MiB holds every decode shape on a 148-SM B200.
+static constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;  // 32 MiB
 static constexpr size_t kNoAllocStatusBytes = 256;
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
@@ -1072,15 +1091,28 @@ int b2g_debug_force_stall(int on) {
   return B2G_OK;
 }
 
+// Reads the allocating entry points' status word and, once b2g_gemm_mxfp8_noalloc
+// has run on this device, the no-alloc array's: the first nonzero one is reported.
+// Allocates nothing, so a caller of the no-alloc entry point may use it too.
 int b2g_device_status(int* status, int clear) {
   if (!status) return fail(B2G_ERR_INVALID_ARG, "null status pointer");
   DevState* d = nullptr;
-  int rc = device_state(&d);
+  int dev = 0;
+  int rc = device_state(&d, &dev);
   if (rc) return rc;
+  int* na_status = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_noalloc[dev].ready) na_status = reinterpret_cast<int*>(g_noalloc[dev].base);
+  }
   B2G_CUDA(cudaDeviceSynchronize());
-  B2G_CUDA(cudaMemcpy(status, d->status, sizeof(int), cudaMemcpyDeviceToHost));
+  int st = 0, na = 0;
+  B2G_CUDA(cudaMemcpy(&st, d->status, sizeof(int), cudaMemcpyDeviceToHost));
+  if (na_status) B2G_CUDA(cudaMemcpy(&na, na_status, sizeof(int), cudaMemcpyDeviceToHost));
+  *status = st ? st : na;
   if (clear) {
-    B2G_CUDA(cudaMemset(d->status, 0, sizeof(int)));
+    if (st) B2G_CUDA(cudaMemset(d->status, 0, sizeof(int)));
+    if (na) B2G_CUDA(cudaMemset(na_status, 0, sizeof(int)));
     // a launch that stopped early can leave tile counters mid-count
     if (*status) B2G_CUDA(cudaMemset(d->tile_cnt, 0, sizeof(unsigned long long) * kSkinnyMaxTiles));
   }
@@ -1372,30 +1404,25 @@ int b2g_gemm_mxfp8_noalloc(const b2g_mxfp8_args* g, void* stream) {
   Env e;
   int rc = noalloc_env(&e);
   if (rc) return rc;
-  // reject up front, before any device work is queued, if the partials do not fit
+  // reject up front, before any device work is queued, if the scratch does not fit
   int bn = 0, S = 1, kb_per = 1;
   rc = plan_tiles(r, e.sms, &bn, &S, &kb_per);
   if (rc) return rc;
   const size_t need = split_ws_bytes(r, S, e.sms);
-  if (need > e.fixed_ws_bytes)
+  if (need > e.fixed_ws_bytes) {
+    if (use_skinny(r, e.sms))
+      return fail(B2G_ERR_WORKSPACE,
+                  "b2g_gemm_mxfp8_noalloc: M=%d takes the decode kernel, whose piece slots need %zu bytes; "
+                  "the fixed scratch array holds %zu", r.M, need, e.fixed_ws_bytes);
     return fail(B2G_ERR_WORKSPACE,
-                "b2g_gemm_mxfp8_noalloc: %d-way split-K partials need %zu bytes; its fixed scratch holds %zu "
-                "(use a smaller log2_k_split, fp32 output, or b2g_gemm_mxfp8)", S, need, e.fixed_ws_bytes);
-  // the status word must start at zero; the partials are fully overwritten
-  B2G_CUDA(cudaMemsetAsync(e.status, 0, sizeof(int), r.stream));
-  rc = run_gemm(r, &e);
-  if (rc) return rc;
-  static const bool sync_check = [] {
-    const char* v = getenv("B2G_SYNC_CHECK");
-    return v && v[0] == '1';
-  }();
-  if (sync_check) {
-    int st = 0;
-    B2G_CUDA(cudaStreamSynchronize(r.stream));
-    B2G_CUDA(cudaMemcpy(&st, e.status, sizeof(int), cudaMemcpyDeviceToHost));
-    if (st) return fail(B2G_ERR_DEVICE_TIMEOUT, "kernel reported device status %d", st);
+                "b2g_gemm_mxfp8_noalloc: %d-way split-K partials (S*M*N*4) need %zu bytes; the fixed scratch "
+                "array holds %zu (use a smaller log2_k_split, or b2g_gemm_mxfp8)", S, need, e.fixed_ws_bytes);
   }
-  return B2G_OK;
+  // Every slot and partial the kernels read is written earlier in the same call,
+  // so nothing in the array needs zeroing per call.  The status word is sticky
+  // (a timeout stays visible to b2g_device_status until cleared there);
+  // B2G_SYNC_CHECK=1 checks it inside run_gemm.
+  return run_gemm(r, &e);
 }
 
 // ------------------------------------------------------------ layout helpers

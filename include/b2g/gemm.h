@@ -255,17 +255,24 @@ B2G_API int b2g_gemm_mxfp8_a2a_out(const b2g_mxfp8_args* args, void* const* peer
  * scratch).  Some hosts hand all of the GPU's memory to their own pool at start-up
  * (serving engines, frameworks with a caching allocator): a cudaMalloc made inside
  * a library either fails for lack of free memory or hides memory the pool cannot
- * account for or reclaim.  This entry point allocates nothing: the split-K fp32
- * partials (bf16 output with log2_k_split > 0) live in a fixed 16 MiB array that
- * the library declares at file scope, which every GPU that loads the library holds
- * until the process exits.  The caller still passes A, B, the scales and D.
- *   - The first call on a device looks up that array's device address; make that
- *     first call before any stream capture.
- *   - Split-K partials needing more than 16 MiB - 256 B (S * M * N * 4 bytes) are
- *     rejected with B2G_ERR_WORKSPACE before any device work is queued.
- *   - Every call on a device shares the one array: calls that overlap on the GPU
- *     (concurrent streams) race on it and must be serialised by the caller.
- * It never calls cudaMalloc, cudaFree or any allocating routine. */
+ * account for or reclaim.  This entry point allocates nothing: its scratch lives
+ * in a fixed 32 MiB array that the library declares at file scope, which every GPU
+ * that loads the library holds until the process exits.  The caller still passes
+ * A, B, the scales and D.  What the array holds:
+ *   - M <= 128 (the decode kernel): fp32 piece slots of its split tiles,
+ *     2 * grid * MP * 128 * 4 bytes (MP = M rounded up to 16/32/64/128, grid <= the
+ *     SM count): at most 18.5 MiB on a 148-SM B200, so every decode shape fits;
+ *   - M > 128 with log2_k_split > 0 and bf16 output: the split-K fp32 partials,
+ *     S * M * N * 4 bytes.  fp32 output adds its partials into D and needs none.
+ *   - the first 256 bytes: the status word its kernels' bounded waits write.  It is
+ *     sticky: b2g_device_status reports it (and, with clear, resets it), and that
+ *     call allocates nothing either.
+ * Scratch needs above 32 MiB - 256 B are rejected with B2G_ERR_WORKSPACE before any
+ * device work is queued.  The first call on a device looks up that array's device
+ * address; make that first call before any stream capture.  Every call on a device
+ * shares the one array: calls that overlap on the GPU (concurrent streams) race on
+ * it and must be serialised by the caller.  It never calls cudaMalloc, cudaFree or
+ * any allocating routine. */
 B2G_API int b2g_gemm_mxfp8_noalloc(const b2g_mxfp8_args* args, void* stream);
 
 /* ------------------------------------------------- tile selection / manifest */
@@ -317,7 +324,10 @@ B2G_API int b2g_quant_128x128(const float* x, int n, int k, void* q, float* sf, 
 
 /* ------------------------------------------------------------ diagnostics */
 /* Synchronises the current device and reports (and with clear != 0 resets) the
- * device status word the kernels write when a bounded wait gives up. */
+ * device status word the kernels write when a bounded wait gives up: the
+ * allocating entry points' word, or else b2g_gemm_mxfp8_noalloc's.  A nonzero
+ * word cleared here also zeroes the decode kernel's tile counters.  Allocates
+ * nothing (both words are file-scope device data). */
 B2G_API int b2g_device_status(int* status, int clear);
 /* Per-wait time limit of the kernels' barrier waits, in milliseconds (default 4000). */
 B2G_API int b2g_set_wait_timeout_ms(int ms);
