@@ -5,16 +5,20 @@
  * and bench.py's CPU-baseline leg compare the CUDA path against.  Nothing in the
  * product library (gcnasm_b200/) links, loads or calls it.
  *
- * Parity status: partially pinned.
+ * Parity status: pinned.
  *   - The f4gemm conventions restated here (E8M0 decode, scale pad+shuffle,
  *     16x16 B preshuffle, f64 reference GEMM) are checked byte-for-byte against
  *     the reference's own f4gemm_ref.hpp compiled from its sources into
  *     oracle/_ref (see oracle/Makefile) and against the golden fixtures in
  *     tests/golden/ that were generated from it.
  *   - The opus gemm_ref loops (block_scale_gemm, block_scale_1x128x1_gemm,
- *     fp8_gemm) cannot be compiled here (they need hipcc, hip_fp8.h and the
- *     aiter OPUS headers); they are restated loop-for-loop with citations, and
- *     the reference ships no golden vectors for them.
+ *     fp8_gemm, opus_fmm's flatmm) are restated loop-for-loop below; the
+ *     reference's own loops are cut unchanged out of its host sources and
+ *     compiled with an E4M3 stand-in for __hip_fp8_e4m3
+ *     (oracle/extract_gemm_ref.py -> oracle/_ref/libopus_ref.so), and the
+ *     restatements equal them bit for bit (fixtures:
+ *     tests/golden/opus_gemm_ref_golden.npz).  The whole host programs cannot
+ *     be compiled here (hipcc, hip/hip_fp8.h and the aiter OPUS headers).
  *
  * Every function cites the reference file:line it follows (paths relative to
  * the reference project root).
@@ -383,7 +387,7 @@ ORC_API void orc_gemm_a8w8_kn(const uint8_t* a, const uint8_t* b, float* c, int 
  * make_operand dequant of asm_f4gemm/f4gemm_ref.hpp:167-173 with E4M3 in place
  * of the e2m1 LUT), then D = alpha * A.B^T accumulated like
  * f4gemm_ref.hpp:181-222.  acc_f64 = 1 reproduces reference_gemm's double
- * accumulation; 0 accumulates in fp32 (the BASELINE acceptance oracle).
+ * accumulation; 0 accumulates in fp32 (the fp32-accumulate acceptance form).
  * sfa/sfb are plain row-major [rows, sf_ld] UE8M0 (sf_ld >= ceil(K/32)). */
 ORC_API void orc_gemm_mx(const uint8_t* a, const uint8_t* b, const uint8_t* sfa, const uint8_t* sfb,
                          int m, int n, int k, int lda, int ldb, int sfa_ld, int sfb_ld,

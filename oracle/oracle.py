@@ -10,7 +10,10 @@ Two shared objects sit behind it:
   reference's CPU GEMMs, formats, quantisers and layout shuffles;
 * ``oracle/_ref/libf4gemm_ref.so`` -- the reference's own ``asm_f4gemm`` host
   code compiled from its sources (present only where the reference tree was
-  available at build time; see ``oracle/Makefile``).
+  available at build time; see ``oracle/Makefile``);
+* ``oracle/_ref/libopus_ref.so`` -- the reference's own opus CPU ``gemm_ref``
+  loops, cut unchanged out of its host sources (``oracle/extract_gemm_ref.py``)
+  and compiled with an E4M3 stand-in for ``__hip_fp8_e4m3`` (same condition).
 """
 from __future__ import annotations
 
@@ -23,12 +26,22 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 _LIB = None
 _REF = None
+_OPUS = None
 
 u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
 f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 f64p = np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")
 u64p = np.ctypeslib.ndpointer(np.uint64, flags="C_CONTIGUOUS")
 i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+
+
+def reference_root() -> str | None:
+    """The reference project tree, where this machine has it: $B2G_REFERENCE_ROOT,
+    else a directory named ``reference`` beside this repository's root; None when
+    neither exists (the checkers then use the prebuilt oracle/_ref libraries and the
+    committed golden fixtures)."""
+    cand = os.environ.get("B2G_REFERENCE_ROOT") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+    return cand if os.path.isdir(cand) else None
 
 
 def build(reference_root: str | None = None) -> None:
@@ -100,6 +113,24 @@ def ref_lib() -> C.CDLL | None:
         R.ref_load_configs.argtypes = [C.c_char_p, ci, i32p, i32p, i32p, i32p]; R.ref_load_configs.restype = ci
         _REF = R
     return _REF
+
+
+def opus_ref_lib() -> C.CDLL | None:
+    """The reference's own opus gemm_ref loops (None when oracle/_ref was not built)."""
+    global _OPUS
+    if _OPUS is None:
+        path = os.path.join(HERE, "_ref", "libopus_ref.so")
+        if not os.path.exists(path):
+            return None
+        R = C.CDLL(path)
+        ci = C.c_int
+        R.ref_opus_blockscale.argtypes = [u8p, u8p, f32p, f32p, f32p] + [ci] * 11
+        R.ref_opus_blockscale_1x128x1.argtypes = [u8p, u8p, f32p, f32p, f32p] + [ci] * 11
+        R.ref_opus_fp8_gemm.argtypes = [u8p, u8p, f32p] + [ci] * 6
+        R.ref_opus_flatmm.argtypes = [u8p, u8p, f32p] + [ci] * 6
+        R.ref_opus_e4m3_to_f32.argtypes = [C.c_uint8]; R.ref_opus_e4m3_to_f32.restype = C.c_float
+        _OPUS = R
+    return _OPUS
 
 
 # --------------------------------------------------------------------------- formats
@@ -254,6 +285,92 @@ def fp4_operand(rows: int, K: int, seed: int):
     return packed, scales
 
 
+def encode_e4m3(x: np.ndarray) -> np.ndarray:
+    """fp32 -> OCP E4M3 bytes, round to nearest even, saturating (the reference
+    hosts' static_cast<host_fp8_t>(float))."""
+    L = lib()
+    flat = np.ascontiguousarray(x, dtype=np.float32).ravel()
+    return np.array([L.orc_f32_to_e4m3(float(v)) for v in flat], dtype=np.uint8).reshape(np.shape(x))
+
+
+def opus_case(loop: str, recipe: str, M: int, N: int, K: int, seed: int) -> dict:
+    """Seeded operands for one of the reference's opus gemm_ref loops.
+
+    loop: "blockscale" (GROUP_N=128, SFB [N/128, K/128]), "blockscale_1x128x1"
+    (GROUP_N=1, SFB [K/128, N]), "fp8_gemm" (no scales, B [N, K]) or "flatmm"
+    (no scales, B [K, N]).  recipe:
+      "uniform" -- the reference hosts' own data: A = E4M3(U[0,1)), B = E4M3(U[-.5,.5)),
+                   fp32 scales U[.8,1.2) (block_scale_gemm/..._host.cc:206-209,
+                   fp8_gemm/gemm_a8w8_8wave.cc:698-699); numpy's seeded generator
+                   stands in for their unseeded std::mt19937;
+      "normal"  -- N(0,1) rows quantised with the 1x128 / 128x128 (or per-column)
+                   amax/448 recipe the benchmarks use (block-scale loops only);
+      "bytes"   -- every finite E4M3 byte (0x00-0x7E with either sign: subnormals,
+                   the largest value 448, negative zero) and scales over [2^-8, 2^8).
+    Returns the operands and the loop's integer arguments."""
+    rs = np.random.RandomState(seed)
+    G = K // 128
+    scaled = loop.startswith("blockscale")
+    gn = 1 if loop == "blockscale_1x128x1" else 128
+    b_rows, b_cols = (K, N) if loop == "flatmm" else (N, K)
+    out = {"loop": loop, "M": M, "N": N, "K": K, "group_n": gn}
+    if recipe == "uniform":
+        a = encode_e4m3(rs.uniform(0.0, 1.0, (M, K)).astype(np.float32))
+        b = encode_e4m3(rs.uniform(-0.5, 0.5, (b_rows, b_cols)).astype(np.float32))
+        sfa = rs.uniform(0.8, 1.2, (G, M)).astype(np.float32)
+        sfb = rs.uniform(0.8, 1.2, (N // 128, G) if gn == 128 else (G, N)).astype(np.float32)
+    elif recipe == "normal":
+        if not scaled:
+            raise ValueError("the normal recipe is for the block-scale loops")
+        a, sfa = quant_1x128(normal_rows(seed, 0, M, K))
+        w = normal_rows(seed + 1, 0, N, K)
+        if gn == 128:
+            b, sfb = quant_128x128(w)
+        else:  # per-column weight scales: a 1x128 quantiser over B's rows, [K/128, N]
+            b, sfb = quant_1x128(w)
+    elif recipe == "bytes":
+        mag = rs.randint(0, 0x7F, (M, K)).astype(np.uint8)
+        a = mag | (rs.randint(0, 2, (M, K)) * 0x80).astype(np.uint8)
+        mag = rs.randint(0, 0x7F, (b_rows, b_cols)).astype(np.uint8)
+        b = mag | (rs.randint(0, 2, (b_rows, b_cols)) * 0x80).astype(np.uint8)
+        sfa = np.exp2(rs.uniform(-8, 8, (G, M))).astype(np.float32)
+        sfb = np.exp2(rs.uniform(-8, 8, (N // 128, G) if gn == 128 else (G, N))).astype(np.float32)
+    else:
+        raise ValueError(recipe)
+    out["a"], out["b"] = np.ascontiguousarray(a), np.ascontiguousarray(b)
+    if scaled:
+        out["sfa"], out["sfb"] = np.ascontiguousarray(sfa), np.ascontiguousarray(sfb)
+        out["stride_sfa"] = M
+        out["stride_sfb"] = G if gn == 128 else N
+    return out
+
+
+def run_opus_case(case: dict, which: str = "oracle") -> np.ndarray:
+    """Run the oracle's restated loop (which="oracle") or the reference's own
+    compiled gemm_ref (which="reference") on an opus_case; fp32 C [M, N]."""
+    M, N, K, loop = case["M"], case["N"], case["K"], case["loop"]
+    c = np.empty((M, N), dtype=np.float32)
+    if which == "oracle":
+        L = lib()
+        fns = {"blockscale": L.orc_gemm_blockscale, "blockscale_1x128x1": L.orc_gemm_blockscale_1x128x1,
+               "fp8_gemm": L.orc_gemm_a8w8, "flatmm": L.orc_gemm_a8w8_kn}
+    else:
+        R = opus_ref_lib()
+        if R is None:
+            raise RuntimeError("oracle/_ref/libopus_ref.so is not built")
+        fns = {"blockscale": R.ref_opus_blockscale, "blockscale_1x128x1": R.ref_opus_blockscale_1x128x1,
+               "fp8_gemm": R.ref_opus_fp8_gemm, "flatmm": R.ref_opus_flatmm}
+    fn = fns[loop]
+    if loop.startswith("blockscale"):
+        fn(case["a"], case["b"], case["sfa"], case["sfb"], c, M, N, K, K, K, N, case["stride_sfa"],
+           case["stride_sfb"], 1, case["group_n"], 128)
+    elif loop == "fp8_gemm":
+        fn(case["a"], case["b"], c, M, N, K, K, K, N)
+    else:
+        fn(case["a"], case["b"], c, M, N, K, K, N, N)
+    return c
+
+
 # --------------------------------------------------------------------------- layouts
 def shuffle_weight_16x16(src: np.ndarray, N: int, Kp: int) -> np.ndarray:
     dst = np.empty(N * Kp, dtype=np.uint8)
@@ -290,7 +407,7 @@ def max_threads() -> int:
 
 # --------------------------------------------------------------------------- tolerances
 def check_bf16(got_f32: np.ndarray, ref: np.ndarray) -> float:
-    """BASELINE acceptance for bf16 C: max|err| <= 2^-7 * max_n |ref[m, n]| per row.
+    """Acceptance for bf16 C: max|err| <= 2^-7 * max_n |ref[m, n]| per row.
     Returns the worst ratio err / bound (pass when <= 1)."""
     ref = np.asarray(ref, dtype=np.float64)
     err = np.abs(np.asarray(got_f32, dtype=np.float64) - ref)
@@ -299,7 +416,7 @@ def check_bf16(got_f32: np.ndarray, ref: np.ndarray) -> float:
 
 
 def check_f32(got: np.ndarray, ref: np.ndarray) -> float:
-    """BASELINE acceptance for fp32 C: |err| / max(|ref|, 2^-7 * rowmax) <= 1e-3.
+    """Acceptance for fp32 C: |err| / max(|ref|, 2^-7 * rowmax) <= 1e-3.
     Returns the worst relative error."""
     ref = np.asarray(ref, dtype=np.float64)
     err = np.abs(np.asarray(got, dtype=np.float64) - ref)

@@ -1,7 +1,7 @@
 """GPU parity: every kernel path through the C ABI against the CPU oracle on the
 same seeded inputs.
 
-Tolerances (written here as asserted):
+Tolerances (the acceptance bounds of this library, written here as asserted):
   * bf16 C:  max |err| <= 2^-7 * max_n |ref[m, n]|     per row   (check_bf16 <= 1)
   * fp32 C:  |err| / max(|ref|, 2^-7 * rowmax) <= 1e-3            (check_f32 <= 1e-3)
   * quantisers, layout shuffles: bit-exact.

@@ -39,10 +39,15 @@ def test_kernel_args_bytes_match_reference(golden):
     assert np.array_equal(mine, golden["fill_args"])
 
 
-@pytest.mark.skipif(not os.path.isdir(os.environ.get("B2G_REFERENCE_ROOT", "/root/reference") + "/opus_gemm"),
+def _reference_root():
+    from oracle import oracle as O
+    return O.reference_root()
+
+
+@pytest.mark.skipif(not (_reference_root() and os.path.isdir(os.path.join(_reference_root(), "opus_gemm"))),
                     reason="reference tree not present")
 def test_c_header_layouts_match_reference_headers():
-    ref = os.environ.get("B2G_REFERENCE_ROOT", "/root/reference")
+    ref = _reference_root()
     src = r'''
 #include <cstddef>
 #include <cstdio>

@@ -228,3 +228,60 @@ def test_against_live_reference(oracle):
         d = np.empty(sm * sn, np.uint8)
         R.ref_shuffle_scale(src, rows, cols, sm, sn, d)
         assert np.array_equal(d, oracle.shuffle_scale(src, rows, cols, sm, sn))
+
+
+# ------------------------------------------------------------ opus gemm_ref loops, pinned
+def _golden_opus_cases():
+    import os
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "opus_gemm_ref_golden.npz")
+    g = np.load(path)
+    out = []
+    for i, spec in enumerate(g["cases"]):
+        loop, recipe, M, N, K, seed = str(spec).split("|")
+        M, N, K = int(M), int(N), int(K)
+        case = {"loop": loop, "M": M, "N": N, "K": K, "group_n": 1 if loop == "blockscale_1x128x1" else 128,
+                "a": g[f"{i}_a"], "b": g[f"{i}_b"]}
+        if loop.startswith("blockscale"):
+            case["sfa"], case["sfb"] = g[f"{i}_sfa"], g[f"{i}_sfb"]
+            case["stride_sfa"] = M
+            case["stride_sfb"] = K // 128 if case["group_n"] == 128 else N
+        out.append((f"{loop}|{recipe}", case, g[f"{i}_c"]))
+    return out, g
+
+
+def test_opus_oracle_matches_reference_golden(oracle):
+    """orc_gemm_blockscale / _1x128x1 / orc_gemm_a8w8 / orc_gemm_a8w8_kn equal, bit for
+    bit, the outputs of the reference's own gemm_ref loops (compiled from its
+    sources by oracle/Makefile; fixtures from tests/golden/make_golden_opus.py)."""
+    cases, _ = _golden_opus_cases()
+    assert len(cases) == 10
+    for name, case, ref in cases:
+        got = oracle.run_opus_case(case, "oracle")
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), name
+
+
+def test_opus_e4m3_stand_in_matches_torch(oracle):
+    """The stand-in for __hip_fp8_e4m3's conversion the reference loops were compiled
+    with decodes like torch's float8_e4m3fn and the oracle's table."""
+    _, g = _golden_opus_cases()
+    t = torch.arange(256, dtype=torch.uint8).view(torch.float8_e4m3fn).float().numpy()
+    mine = oracle.e4m3_table()
+    for table in (g["e4m3"], mine):
+        assert np.array_equal(np.isnan(table), np.isnan(t))
+        ok = ~np.isnan(t)
+        assert np.array_equal(table[ok].view(np.uint32), t[ok].view(np.uint32))
+
+
+@pytest.mark.skipif(__import__("oracle.oracle", fromlist=["x"]).opus_ref_lib() is None,
+                    reason="oracle/_ref/libopus_ref.so not built (reference tree absent)")
+@pytest.mark.parametrize("loop", ["blockscale", "blockscale_1x128x1", "fp8_gemm", "flatmm"])
+def test_opus_oracle_matches_live_reference(oracle, loop):
+    """The same pin against the live compiled reference on more shapes and seeds:
+    ragged M, several K groups, each data recipe."""
+    recipes = ["uniform", "bytes"] + (["normal"] if loop.startswith("blockscale") else [])
+    for recipe in recipes:
+        for (M, N, K), seed in (((1, 128, 128), 1), ((37, 256, 640), 2), ((64, 384, 1024), 3)):
+            case = oracle.opus_case(loop, recipe, M, N, K, seed)
+            got = oracle.run_opus_case(case, "oracle")
+            ref = oracle.run_opus_case(case, "reference")
+            assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), (recipe, M, N, K)
