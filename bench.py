@@ -120,12 +120,32 @@ def cpu_gemm_sample(M, N, K, budget_s=12.0, seed=0):
     O.gemm_mx(qa, qb, sa, sb, probe, N, K, acc_f64=False)
     dt = time.perf_counter() - t
     rows = int(max(probe, min(M, probe * budget_s / max(dt, 1e-6))))
+    if rows < M and M * dt / probe <= 2.5 * budget_s:  # the whole GEMM fits: run all of it
+        rows = M
     qa, sa = O.quant_mx(O.normal_rows(1234, 0, rows, K))
     t = time.perf_counter()
     O.gemm_mx(qa, qb, sa, sb, rows, N, K, acc_f64=False)
     dt = time.perf_counter() - t
     del np
     return 2.0 * rows * N * K / dt / 1e12, rows, O.max_threads(), dt
+
+
+def cpu_decode(M, N, K):
+    """The oracle port on the whole M=16 decode GEMM (C4, fp32 out): HBM-style GB/s of
+    the algorithmic bytes and the time, on the host cores."""
+    from oracle import oracle as O
+
+    qa, sa = O.quant_mx(O.normal_rows(1234, 0, M, K))
+    qb, sb = O.quant_mx(O.normal_rows(5678, 0, N, K))
+    O.gemm_mx(qa, qb, sa, sb, M, N, K, acc_f64=False)  # warm (threads, table)
+    reps, t = 3, time.perf_counter()
+    for _ in range(reps):
+        O.gemm_mx(qa, qb, sa, sb, M, N, K, acc_f64=False)
+    dt = (time.perf_counter() - t) / reps
+    nbytes = M * K + N * K + M * K // 32 + N * K // 32 + 4 * M * N
+    return {"M": M, "N": N, "K": K, "us_per_call": round(dt * 1e6, 1), "gbs": round(nbytes / dt / 1e9, 3),
+            "tflops": round(2.0 * M * N * K / dt / 1e12, 5), "cores": O.max_threads(),
+            "sample": "the whole GEMM, mean of 3 runs"}
 
 
 # --------------------------------------------------------------------------- GPU legs
@@ -251,12 +271,21 @@ def run_b200(args, rank, world, local_rank):
     result["decode"] = bench_decode(args, dev, stream, peaks, flush)
     # ---------------------------------------------------------------- MXFP4 (the f4gemm element type)
     result["mxfp4"] = bench_mxfp4(args, dev, stream, peaks, flush)
+    # ---------------------------------------------------------------- C3: the block-scale GEMMs
+    result["blockwise"] = bench_blockwise(args, dev, stream, peaks, flush)
+    # ---------------------------------------------------------------- a measured FP8 tensor peak
+    fp8 = bench_fp8_peak(args, dev, stream, flush)
+    result["fp8_peak_cublas"] = fp8
+    if "tflops_best" in fp8:
+        result["roofline"]["frac_of_cublas_fp8"] = round(achieved / fp8["tflops_best"], 4)
     # ---------------------------------------------------------------- CPU baseline (oracle port, N=1)
     if world == 1:
         tf, rows, cores, secs = cpu_gemm_sample(M, N, K, budget_s=args.cpu_budget)
+        whole = "the whole GEMM" if rows == M else f"{rows} of its {M} rows (time extrapolates linearly in M)"
         result["cpu_baseline"] = {"value": round(tf, 5), "unit": "TFLOP/s", "cores": cores, "kind": "port",
-                                  "sample": f"{rows} rows x {N} x {K} of the same GEMM ({secs:.1f} s, fp32 "
-                                            "accumulate, OpenMP over rows; extrapolates linearly in M)"}
+                                  "sample": f"{whole}: {rows} x {N} x {K} in {secs:.1f} s, fp32 accumulate, "
+                                            "OpenMP over rows",
+                                  "decode": cpu_decode(16, 28672, 4096)}
     del capi, f4gemm
     return result
 
@@ -483,6 +512,97 @@ def bench_mxfp4(args, dev, stream, peaks, flush):
             "gpu_launches_per_call": 1}
 
 
+C3_NK = ((7168, 2048), (4096, 7168), (7168, 18432))
+C3_M = (128, 1024, 4096, 16384)
+
+
+def blockwise_bytes(M, N, K):
+    """Algorithmic bytes of a 1x128 / 128x128 block-scale GEMM with bf16 C: A, B, the
+    fp32 1x128 scales of A, the fp32 128x128 scales of B, C."""
+    return M * K + N * K + 4 * M * (K // 128) + 4 * (N // 128) * (K // 128) + 2 * M * N
+
+
+def bench_blockwise(args, dev, stream, peaks, flush):
+    """C3: the 1x128x1 block-scale GEMM (E4M3 A and B, fp32 scale per 1x128 of A and
+    per 128x128 tile of B -- or per column with GROUP_N=1 -- bf16 C) at all twelve
+    shapes, one kernel launch per call, L2 flushed between calls.  Each shape is
+    judged against the roofline that binds it: HBM where its arithmetic intensity
+    is below the ridge (peak FLOP/s / HBM B/s), the FP8 tensor peak above."""
+    import torch
+
+    from gcnasm_b200 import ops
+
+    fp8_peak = 2.0 * peaks["bf16_tflops"]
+    ridge = fp8_peak * 1e12 / (peaks["hbm_gbs"] * 1e9)
+    reps = max(5, min(args.steps, 20))
+    out_rows = []
+    for N, K in C3_NK:
+        w = torch.randn(N, K, device=dev, generator=torch.Generator(device=dev).manual_seed(601 + N + K))
+        wq = {128: ops.quant_128x128(w), 1: ops.quant_1x128(w)}
+        del w
+        for M in C3_M:
+            x = torch.randn(M, K, device=dev, generator=torch.Generator(device=dev).manual_seed(701 + M))
+            qa, sfa = ops.quant_1x128(x)
+            del x
+            out = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+            flops, nbytes = 2.0 * M * N * K, blockwise_bytes(M, N, K)
+            bound = "tensor" if flops / nbytes > ridge else "hbm"
+            for gn in (128, 1):
+                qb, sfb = wq[gn]
+
+                def step():
+                    ops.gemm_a8w8_blockscale(qa, qb, sfa, sfb, group_n=gn, out=out, stream=stream)
+
+                step()
+                torch.cuda.synchronize()
+                ms = statistics.mean(timed_steps(step, reps, 3, flush, stream))
+                tf, gbs = flops / (ms * 1e-3) / 1e12, nbytes / (ms * 1e-3) / 1e9
+                kern = ("b2g_gemm_skinny_blk_kernel" if (M <= 32 and N // 128 > 148) else
+                        f"b2g_gemm_kernel<Blk,{128 if M <= 128 else 256}>")
+                out_rows.append({
+                    "M": M, "N": N, "K": K, "group_n": gn, "us_per_call": round(ms * 1e3, 2),
+                    "tflops": round(tf, 1), "hbm_gbs": round(gbs, 1), "algorithmic_flop": flops,
+                    "algorithmic_bytes": nbytes, "bound": bound,
+                    "frac": round(tf / fp8_peak if bound == "tensor" else gbs / peaks["hbm_gbs"], 4),
+                    "kernel": kern})
+            del qa, sfa, out
+        del wq
+        torch.cuda.empty_cache()
+    return {"out": "bf16", "l2": "flushed between calls (256 MiB write, outside the events)",
+            "reps_per_shape": reps, "fp8_peak_tflops": round(fp8_peak, 1), "hbm_peak_gbs": peaks["hbm_gbs"],
+            "ridge_flop_per_byte": round(ridge, 1),
+            "peak_source": f"{peaks['source']}: FP8 = bf16 dense x2; HBM = copy bandwidth",
+            "shapes": out_rows}
+
+
+def bench_fp8_peak(args, dev, stream, flush):
+    """A measured dense-FP8 tensor-core reference beside the derived one: cuBLAS
+    (torch._scaled_mm, per-tensor scales, E4M3 x E4M3 -> bf16) at 8192^3 on this GPU,
+    burst (best of the timed calls, L2 flushed between them)."""
+    import torch
+
+    M = N = K = 8192
+    try:
+        a = torch.randn(M, K, device=dev).to(torch.float8_e4m3fn)
+        b = torch.randn(N, K, device=dev).to(torch.float8_e4m3fn)
+        one = torch.ones((), device=dev)
+
+        def step():
+            torch._scaled_mm(a, b.t(), scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+
+        step()
+        torch.cuda.synchronize()
+        times = timed_steps(step, max(10, min(args.steps, 30)), 3, flush, stream)
+        best = min(times)
+        del a, b
+        return {"tflops_best": round(2.0 * M * N * K / (best * 1e-3) / 1e12, 1),
+                "tflops_mean": round(2.0 * M * N * K / (statistics.mean(times) * 1e-3) / 1e12, 1),
+                "how": "torch._scaled_mm (cuBLAS) E4M3 8192^3 -> bf16, per-tensor scales, CUDA events, "
+                       "L2 flushed between calls"}
+    except Exception as e:  # an unsupported build leaves the derived peak as the only one
+        return {"error": f"{type(e).__name__}: {e}"[:300]}
+
+
 def bench_e2e(args, dev, stream, qa, sfa_rm, qb, sfb_rm, M, N, K):
     """The reference-facing call (b2g_gemm_mxfp8_f4gemm over the f4gemm kernarg
     block, B 16x16-preshuffled, scales padded + shuffled) with pinned host
@@ -555,29 +675,36 @@ def bench_e2e(args, dev, stream, qa, sfa_rm, qb, sfb_rm, M, N, K):
 
 
 def run_reference(args, rank):
-    """The reference's CPU GEMM path (oracle port; the reference itself needs hipcc
-    and aiter, absent here) on the box's host cores, bounded sample per step."""
+    """The reference's CPU GEMM path on the box's host cores: the oracle port of its
+    loops (bit-identical to the reference's own loops compiled here; the reference
+    host programs themselves need hipcc and aiter, absent here).  Each step is a
+    bounded row sample of the 8192^3 GEMM; ms_per_step is the measured wall time of
+    the work each step actually did, and the full-GEMM time it implies is reported
+    separately."""
     if rank != 0:
         return None
     M = N = K = 8192
-    vals = []
     for _ in range(args.warmup):
-        cpu_gemm_sample(M, N, K, budget_s=2.0)
-    rows_used, cores, secs_total = 0, 1, 0.0
+        cpu_gemm_sample(M, N, K, budget_s=1.0)
+    vals, secs, rows_used, cores = [], [], 0, 1
     for _ in range(args.steps):
-        tf, rows, cores, secs = cpu_gemm_sample(M, N, K, budget_s=args.cpu_budget / max(1, args.steps))
+        tf, rows, cores, dt = cpu_gemm_sample(M, N, K, budget_s=args.cpu_budget / max(1, args.steps))
         vals.append(tf)
-        rows_used, secs_total = rows, secs_total + secs
+        secs.append(dt)
+        rows_used = rows
     v = statistics.mean(vals)
+    ms = 1e3 * statistics.mean(secs)
     return {"metric": METRIC, "value": round(v, 5), "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": round(2.0 * M * N * K / (v * 1e12) * 1e3, 1),
+            "warmup": args.warmup, "ms_per_step": round(ms, 1),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "impl": "reference",
             "dtype": "e4m3+ue8m0 (fp32 accumulate), bf16 out", "data": "synthetic N(0,1) seeded (oracle generator)",
             "config": {"workload": "mxfp8_gemm_tn", "M": M, "N": N, "K": K, "out": "bf16",
                        "parallelism": "host cores (OpenMP)"},
+            "step_work": f"{rows_used} rows x {N} x {K} of the {M}-row GEMM per step (ms_per_step is its wall time)",
+            "full_gemm_ms_extrapolated": round(2.0 * M * N * K / (v * 1e12) * 1e3, 1),
             "cpu_baseline": {"value": round(v, 5), "unit": "TFLOP/s", "cores": cores, "kind": "port",
-                             "sample": f"{rows_used} rows x {N} x {K} per step ({secs_total:.1f} s total); "
-                                       "time extrapolated linearly in M"},
+                             "sample": f"{rows_used} rows x {N} x {K} per step, {args.steps} steps "
+                                       f"({sum(secs):.1f} s measured)"},
             "e2e": {"value": round(v, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 

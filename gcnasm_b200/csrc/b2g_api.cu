@@ -235,7 +235,7 @@ constexpr int kManifestN = sizeof(kManifest) / sizeof(kManifest[0]);
 // ceil(tiles * splitK / num_sm); ties go to fewer idle SMs, then to the larger
 // tile_m*tile_n/(tile_m+tile_n); manifest order breaks remaining ties.
 void select_tile(int M, int N, int num_sm, int log2_k_split, int bpreshuffle, int* idx, int* log2_out,
-                 int max_tile_n = 1 << 30, int max_tile_m = 1 << 30) {
+                 int max_tile_n = 1 << 30, int max_tile_m = 1 << 30, int only = -1) {
   uint32_t empty_cu = static_cast<uint32_t>(num_sm);
   uint32_t round = 0xffffffffu;
   float effi = 1.0f;
@@ -244,6 +244,7 @@ void select_tile(int M, int N, int num_sm, int log2_k_split, int bpreshuffle, in
   int sel = -1, sel_split = 1;
   for (int i = 0; i < kManifestN; ++i) {
     const TileCfg& c = kManifest[i];
+    if (only >= 0 && i != only) continue;
     if (c.bpre != bpre_en || c.splitk < split_en || c.tile_n > max_tile_n || c.tile_m > max_tile_m) continue;
     if (c.tile_m == 128 && c.tile_n == 512 && (N % c.tile_n) != 0) continue;
     int cand[4], nc = 0;
@@ -462,6 +463,18 @@ int blk_max_bn(const Req& r) {
   return r.M <= 128 ? 128 : 256;
 }
 
+// B2G_FORCE_TILE=<manifest knl_name>: run that manifest entry (and only its
+// split choices) for every request it can serve -- the analogue of the reference
+// host's `--kernel <co>` (asm_f4gemm/main.cpp), used by the regression sweep.
+// Read at every call.  Returns the entry, -1 when unset, -2 for an unknown name.
+int forced_tile() {
+  const char* v = getenv("B2G_FORCE_TILE");
+  if (!v || !*v) return -1;
+  for (int i = 0; i < kManifestN; ++i)
+    if (!strcmp(kManifest[i].name, v)) return i;
+  return -2;
+}
+
 int plan_tiles(const Req& r, int sms, int* bn_out, int* S_out, int* kb_per_out, int* bm_out = nullptr) {
   int bn = r.bn, l2 = r.log2_k_split, bm = 128;
   if (r.mode == kModeBlk && bn > blk_max_bn(r)) bn = blk_max_bn(r);
@@ -473,9 +486,14 @@ int plan_tiles(const Req& r, int sms, int* bn_out, int* S_out, int* kb_per_out, 
       return v && v[0] == '1';
     }();
     const bool pair_ok = r.M > 128 && r.mode != kModeBlk && !pair_off;
+    const int only = forced_tile();
+    if (only == -2) return fail(B2G_ERR_INVALID_ARG, "B2G_FORCE_TILE names no manifest entry");
     int idx = -1, lsel = 0;
     select_tile(r.M, r.N, sms, r.log2_k_split, r.bpre ? 1 : 0, &idx, &lsel, r.mode == kModeBlk ? blk_max_bn(r) : 1 << 30,
-                pair_ok ? 1 << 30 : 128);
+                pair_ok ? 1 << 30 : 128, only);
+    if (idx < 0 && only >= 0)
+      return fail(B2G_ERR_UNSUPPORTED, "B2G_FORCE_TILE=%s cannot serve this request (B layout, mode or M)",
+                  kManifest[only].name);
     if (idx < 0) return fail(B2G_ERR_UNSUPPORTED, "no tile in the manifest fits");
     bn = kManifest[idx].tile_n;
     bm = kManifest[idx].tile_m;
