@@ -346,7 +346,10 @@ int dispatch_pre_out(const Env& d, bool pre, bool f32, const CUtensorMap& ta, co
   }
   if (epi_any(p.epi) && p.out_mode == kOutStore)
     return fail(B2G_ERR_UNSUPPORTED, "beta * C / bias epilogue: MX modes with 256-wide tiles only");
-  if (kMode == kModeBlk) {  // blockwise path: row-major B only
+  if (kMode == kModeBlk) {  // blockwise path: row-major B only; instances per weight-scale layout
+    if (p.group_n == 1)
+      return f32 ? launch_cfg<GemmCfg<kMode, kBN, false, true, false, true>>(d, ta, tb, p, grid, st)
+                 : launch_cfg<GemmCfg<kMode, kBN, false, false, false, true>>(d, ta, tb, p, grid, st);
     return f32 ? launch_cfg<GemmCfg<kMode, kBN, false, true>>(d, ta, tb, p, grid, st)
                : launch_cfg<GemmCfg<kMode, kBN, false, false>>(d, ta, tb, p, grid, st);
   } else {
@@ -884,7 +887,13 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
   p.group_n = r.group_n;
   p.MT = cdiv(r.M, bm); p.NT = cdiv(r.N, bn);
   p.S = S; p.KB = KB; p.kb_per_split = kb_per;
-  p.group_m = 8;
+  // grouped raster: group_m row tiles walked together down every column tile
+  // (B2G_GROUP_M=<n> overrides, for tuning)
+  static const int group_m_env = [] {
+    const char* v = getenv("B2G_GROUP_M");
+    return v ? atoi(v) : 0;
+  }();
+  p.group_m = group_m_env > 0 ? group_m_env : 8;
   const long long units = static_cast<long long>(r.batch) * p.MT * p.NT * S;
   if (units > 0x7fffffffLL) return fail(B2G_ERR_UNSUPPORTED, "problem too large");
   p.num_units = static_cast<int>(units);
@@ -917,7 +926,11 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
     if (p.out_mode == kOutStore && (r.ldc * es) % 16 == 0 && (bstride * es) % 16 == 0) {
       cuuint64_t dims[3] = {(cuuint64_t)r.N, (cuuint64_t)r.M, (cuuint64_t)r.batch};
       cuuint64_t str[2] = {(cuuint64_t)(r.ldc * es), (cuuint64_t)(bstride * es)};
-      cuuint32_t box[3] = {(cuuint32_t)(64 / es), 32, 1};
+      // boxes of the epilogue's store chunk (GemmCfg::kStoreChunkBytes): 32 bytes of
+      // columns for the 20-warp blockwise tile (256 wide, 128 x 128 weight scales),
+      // 64 for every other kernel
+      const long long chunk = (r.mode == kModeBlk && r.group_n != 1 && !pair && bn == 256) ? 32 : 64;
+      cuuint32_t box[3] = {(cuuint32_t)(chunk / es), 32, 1};
       rc = encode(&p.tm_c, r.out_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, r.c,
                   dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
       if (rc) return rc;

@@ -19,10 +19,11 @@
 //                block_scale_gemm/gemm_a8w8_blockscale_kernel_template.hpp:23-39,
 //                applied to TMEM accumulator tiles.
 //
-// Structure (one CTA per SM, 320 threads):
+// Structure (one CTA per SM, 320 threads; the 256-wide blockwise tile 640):
 //   warp 0      TMA producer: A/B tiles (and MX scale atoms) -> smem ring
 //   warp 1      TMEM owner + single-thread tcgen05.mma issuer
 //   warps 2..9  epilogue: tcgen05.ld -> registers -> scale / convert -> global
+//               (256-wide blockwise: warps 4..11 or 4..19, see GemmCfg::kWide)
 // Tiles are 128 x kBN x 128 (M x N x K).  Work units (batch, m-tile, n-tile,
 // k-split) are walked statically: CTA i takes units i, i + grid, ... in a
 // grouped raster so that concurrently running tiles share A rows in L2.
@@ -181,11 +182,12 @@ __device__ __noinline__ void peer_store_warp(const GemmParams& p, const float (&
 // and staged 64 bytes of columns at a time in the warp's 2 KB of shared memory,
 // each chunk a (64 B x 32 rows) box stored by lane 0.  Rows past M and columns
 // past N are clipped by the store itself, so every lane takes part.
-template <int NC, bool kF32>
+template <int NC, bool kF32, int kChunkBytes = 64>
 __device__ __forceinline__ void tma_store_rows(const CUtensorMap* tm, const float (&acc)[NC], int col0, int row0,
                                                int b, uint8_t* stage, int lane) {
-  constexpr int CH = kF32 ? 16 : 32;  // columns per 64-byte row chunk
-  uint4* mine = reinterpret_cast<uint4*>(stage + lane * 64);
+  constexpr int CH = kChunkBytes / (kF32 ? 4 : 2);  // columns per row chunk
+  constexpr int Q = kChunkBytes / 16;               // 16-byte pieces per row chunk
+  uint4* mine = reinterpret_cast<uint4*>(stage + lane * kChunkBytes);
 #pragma unroll
   for (int c = 0; c < NC / CH; ++c) {
     if (c > 0) {  // the previous chunk's store has read the stage
@@ -193,7 +195,7 @@ __device__ __forceinline__ void tma_store_rows(const CUtensorMap* tm, const floa
       __syncwarp();
     }
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < Q; ++q) {
       if (kF32)
         mine[q] = make_uint4(__float_as_uint(acc[c * CH + 4 * q]), __float_as_uint(acc[c * CH + 4 * q + 1]),
                              __float_as_uint(acc[c * CH + 4 * q + 2]), __float_as_uint(acc[c * CH + 4 * q + 3]));
@@ -234,25 +236,40 @@ __host__ __device__ __forceinline__ Unit decode_unit(int u, const GemmParams& p)
 }
 
 // compile-time configuration -------------------------------------------------
-template <int kMode_, int kBN_, bool kBPre_, bool kOutF32_, bool kEpi_ = false>
+template <int kMode_, int kBN_, bool kBPre_, bool kOutF32_, bool kEpi_ = false, bool kGn1_ = false>
 struct GemmCfg {
   static constexpr int kMode = kMode_;
+  // blockwise: B's fp32 scales per column (GROUP_N = 1) instead of per 128 x 128 block
+  static constexpr bool kGn1 = kGn1_;
   static constexpr bool kEpi = kEpi_;  // beta * C / bias terms compiled in (only the instances that take them)
   static constexpr int kBN = kBN_;
   static constexpr bool kBPre = kBPre_;     // B given 16x16-preshuffled ([N/16][K/16][16][16] bytes)
   static constexpr bool kOutF32 = kOutF32_;
   static constexpr int kBM = 128, kBK = 128, kUmmaK = 32;
-  // The 256-wide blockwise tile keeps 128 fp32 sums per epilogue thread: it runs
-  // 12 warps (warpgroup 0: producer, MMA issuer, two idle warps; warpgroups 1-2:
-  // the 8 epilogue warps) and moves registers from warpgroup 0 (56 each) to the
-  // epilogue (224 each): 128 * 56 + 256 * 224 = 384 * 168, the launch's total.
-  // Every other tile: 10 warps, epilogue warps 2..9.
+  // The 256-wide blockwise tile promotes every 128-K block's 128 x 256 partial in
+  // registers and re-splits the registers between warpgroups (setmaxnreg); the
+  // two weight-scale layouts are separate instances (kGn1), so each epilogue
+  // carries only its own promotion code:
+  //   - 128 x 128 weight scales (kQuad): 20 warps, warpgroup 0 (producer, MMA
+  //     issuer, two idle warps) and 16 epilogue warps, four per TMEM lane group,
+  //     each holding 64 fp32 sums of one row, so a partial buffer drains in half
+  //     the time of 8 warps.  The launch holds 640 * 96 registers; warpgroup 0
+  //     drops to 32, the epilogue rises to 112: 128 * 32 + 512 * 112 = 640 * 96,
+  //     per sub-partition 32 + 4 * 112 <= 512.
+  //   - per-column weight scales: 12 warps, 8 epilogue warps of 128 sums each
+  //     (its column-scale staging does not fit 112 registers without spilling);
+  //     warpgroup 0 at 56, the epilogue at 224: 128 * 56 + 256 * 224 = 384 * 168.
+  // Every other tile: 10 warps, epilogue warps 2..9, each half a tile's columns.
   static constexpr bool kWide = kMode == kModeBlk && kBN_ == 256;
-  static constexpr int kThreads = kWide ? 384 : 320;
+  static constexpr bool kQuad = kWide && !kGn1;
+  static constexpr int kThreads = kQuad ? 640 : (kWide ? 384 : 320);
   static constexpr int kFirstEpiWarp = kWide ? 4 : 2;
-  static constexpr int kEpiWarps = 8;
-  static constexpr int kColsPerThread = kBN / 2;  // each epilogue thread: one row, half the tile
+  static constexpr int kEpiWarps = kQuad ? 16 : 8;
+  static constexpr int kRegsLow = kQuad ? 32 : 56, kRegsHigh = kQuad ? 112 : 224;  // kWide re-split
+  static constexpr int kColsPerThread = kBN / (kEpiWarps / 4);  // each epilogue thread: one row, a column slice
   static constexpr int kChunks = kColsPerThread / 32;
+  // bytes of columns per TMA-store box of C (boxes are that x 32 rows)
+  static constexpr int kStoreChunkBytes = kQuad ? 32 : 64;
 
   static constexpr int kABytes = kBM * kBK;
   static constexpr int kBBytes = kBN * kBK;
@@ -286,7 +303,7 @@ struct GemmCfg {
   static constexpr int kOffSbStage = kOffSfb + kStages * kSfbBytes;  // GROUP_N=1 column scales
   static constexpr int kSbStageBytes = kMode == kModeBlk ? kEpiWarps * kColsPerThread * 4 : 0;
   static constexpr int kOffStageC = (kOffSbStage + kSbStageBytes + 1023) / 1024 * 1024;  // TMA-store staging
-  static constexpr int kStageCBytes = kEpiWarps * 2048;                                     // 2 KB per warp
+  static constexpr int kStageCBytes = kEpiWarps * 32 * kStoreChunkBytes;                  // one box per warp
   static constexpr int kOffBar = (kOffStageC + kStageCBytes + 7) / 8 * 8;
   static constexpr int kNumBars = 2 * kStages + 2 * kAccStages + 2;
   static constexpr int kOffCtl = kOffBar + kNumBars * 8;
@@ -343,7 +360,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
   // compiler allocates the epilogue's code with 224 registers
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
-    if constexpr (Cfg::kWide) setmaxnreg_dec<56>();
+    if constexpr (Cfg::kWide) setmaxnreg_dec<Cfg::kRegsLow>();
     if (lane == 0) {
       tma_prefetch_desc(&tm_a);
       tma_prefetch_desc(&tm_b);
@@ -393,7 +410,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if constexpr (Cfg::kWide) setmaxnreg_dec<56>();
+    if constexpr (Cfg::kWide) setmaxnreg_dec<Cfg::kRegsLow>();
     if (lane == 0) {
       int s = 0, as = 0;
       uint32_t ph = 0, aph = 0, sfbuf = 0;
@@ -465,20 +482,20 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     __syncwarp();
   } else if (warp < Cfg::kFirstEpiWarp) {
     // ------------------------------------------------------------ idle (kWide: the rest of warpgroup 0)
-    if constexpr (Cfg::kWide) setmaxnreg_dec<56>();
+    if constexpr (Cfg::kWide) setmaxnreg_dec<Cfg::kRegsLow>();
   } else {
     // ------------------------------------------------------------ epilogue
-    if constexpr (Cfg::kWide) setmaxnreg_inc<224>();
+    if constexpr (Cfg::kWide) setmaxnreg_inc<Cfg::kRegsHigh>();
     const int ew = warp - Cfg::kFirstEpiWarp;
     const int quad = warp & 3;                 // TMEM lane group this warp may access
-    const int half = ew >> 2;                  // which half of the tile's columns
+    const int half = ew >> 2;                  // which column slice of the tile (half, or quarter when kQuad)
     const int row_in_tile = quad * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
     constexpr int NC = Cfg::kColsPerThread;
     int as = 0;
     uint32_t aph = 0;
     float* sb_stage = reinterpret_cast<float*>(smem + Cfg::kOffSbStage) + ew * NC;
-    uint8_t* stage_c = smem + Cfg::kOffStageC + ew * 2048;
+    uint8_t* stage_c = smem + Cfg::kOffStageC + ew * (32 * Cfg::kStoreChunkBytes);
 
     for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
       const Unit w = decode_unit(u, p);
@@ -510,7 +527,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         for (int j = 0; j < NC; ++j) acc[j] = 0.f;
         const bool row_ok = m < p.M;
         const float* sa_ptr = p.bsa + w.b * p.bsa_bstride + m;
-        const bool gn1 = p.group_n == 1;
+        constexpr bool gn1 = Cfg::kGn1;
         const int nblk = col0 / 128;
         const float* sb_ptr = gn1 ? (p.bsb + w.b * p.bsb_bstride + col0 + 4 * lane)
                                   : (p.bsb + w.b * p.bsb_bstride + nblk * p.stride_sfb);
@@ -583,7 +600,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       }
       // ---- write the row segment [col0, col0 + NC) of row m
       if (p.tma_store && p.out_mode == kOutStore) {
-        tma_store_rows<NC, Cfg::kOutF32>(&p.tm_c, acc, col0, w.mt * 128 + quad * 32, w.b, stage_c, lane);
+        tma_store_rows<NC, Cfg::kOutF32, Cfg::kStoreChunkBytes>(&p.tm_c, acc, col0, w.mt * 128 + quad * 32, w.b,
+                                                                 stage_c, lane);
       } else if (kMode != kModeBlk && p.out_mode == kOutPeers) {  // the peer entry point is MX only
         peer_store_warp<NC, Cfg::kOutF32>(p, acc, w.mt * 128 + quad * 32, col0, w.mt * p.NT + w.nt, stage_c, lane);
       } else if (m < p.M) {
