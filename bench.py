@@ -364,7 +364,45 @@ def bench_c5(args, dev, stream, world, rank, flush):
             "ms_per_step": round(ms_n, 3), "cols_per_gpu": cols, "n_gpus": world,
             "collective": "NCCL all_gather of the bf16 column slabs (M x N/world x 2 B per rank), then the "
                           "[M, N] assembly, inside the timed step"}
-        del c_local
+        # the same gather handed over in the slab layout [world, M, N / world] (no assembly copy)
+        def step_s():
+            shard.n_sharded_allgather(local_gemm, N, world, rank, layout="slabs")
+
+        step_s()
+        torch.cuda.synchronize()
+        dist.barrier()
+        ms_s = max_over_ranks(sum(timed_steps(step_s, steps, 3, flush, stream)) / steps)
+        res["n_shard_allgather_slabs"] = {
+            "value": round(2.0 * M * N * K / (ms_s * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+            "ms_per_step": round(ms_s, 3), "cols_per_gpu": cols, "n_gpus": world,
+            "collective": "NCCL all_gather_into_tensor straight into the [world, M, N/world] slab layout "
+                          "(no assembly copy), inside the timed step"}
+
+        # ... and gathered panel by panel, each panel's gather overlapping the next panel's GEMM
+        panels = 4
+        rows_p = M // panels
+        c_pan = [torch.empty((rows_p, cols), dtype=torch.bfloat16, device=dev) for _ in range(panels)]
+
+        def local_rows(row0, nrows):
+            i = row0 // rows_p
+            ops.mxfp8_gemm(qa[row0:row0 + nrows], qb_local,
+                           sfa[shard.sf_tc_row_offset(row0, K):shard.sf_tc_row_offset(row0 + nrows, K)], sfb_local,
+                           out=c_pan[i], stream=stream)
+            return c_pan[i]
+
+        def step_o():
+            shard.n_sharded_allgather_panels(local_rows, M, N, world, rank, panels=panels)
+
+        step_o()
+        torch.cuda.synchronize()
+        dist.barrier()
+        ms_o = max_over_ranks(sum(timed_steps(step_o, steps, 3, flush, stream)) / steps)
+        res["n_shard_allgather_overlap"] = {
+            "value": round(2.0 * M * N * K / (ms_o * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+            "ms_per_step": round(ms_o, 3), "cols_per_gpu": cols, "n_gpus": world, "panels": panels,
+            "collective": f"the GEMM in {panels} row panels; each panel's NCCL all-gather (async, its own "
+                          "stream) into the slab layout overlaps the next panel's GEMM, inside the timed step"}
+        del c_local, c_pan
         torch.cuda.empty_cache()
 
         # the same with the gather folded into the GEMM epilogue (peer stores over NVLink)

@@ -5,7 +5,8 @@
   so that a shard of the tensor-core scale layout is a pointer offset.
 * N-shard (column parallel): rank g owns columns [col0, col0 + cols) of B / SFB
   / C and A is replicated; the bf16 column slabs are all-gathered over NCCL
-  (NVLink) into [G, M, cols] and transposed locally into [M, N].
+  (NVLink) into [G, M, cols], handed over as that slab layout or re-assembled
+  into [M, N]; or gathered panel by panel while the GEMM computes the next panel.
 * N-shard with the gather folded into the GEMM: every rank's full-width C lives
   in symmetric memory (mapped into every process); each rank's GEMM epilogue
   stores its columns straight into all ranks' C over NVLink, and a one-element
@@ -54,17 +55,56 @@ def m_sharded(local_gemm: Callable[[int, int], torch.Tensor], M: int, world: int
 
 
 def n_sharded_allgather(local_gemm: Callable[[int, int], torch.Tensor], N: int, world: int, rank: int,
-                        group=None) -> torch.Tensor:
-    """Column-parallel GEMM + all-gather of the output slabs -> full C [M, N].
+                        group=None, layout: str = "mn") -> torch.Tensor:
+    """Column-parallel GEMM + all-gather of the output slabs.
 
-    Every rank takes the same collective steps; column shards must be equal-sized
-    (N divisible by 128 * world) so that the slabs stack."""
+    layout "mn": the full C [M, N] (the gathered slabs re-assembled, one copy);
+    layout "slabs": C as gathered, [world, M, N / world] -- slab g holds columns
+    [g * N / world, (g + 1) * N / world) -- written by the collective in place,
+    with no assembly copy.  Every rank takes the same collective steps; column
+    shards must be equal-sized (N divisible by 128 * world)."""
     col0, cols = col_range(N, world, rank)
     assert N % (128 * world) == 0, "N-shard needs N divisible by 128 * world"
+    assert layout in ("mn", "slabs")
     c_local = local_gemm(col0, cols).contiguous()  # [M, cols]
-    slabs = [torch.empty_like(c_local) for _ in range(world)]
-    dist.all_gather(slabs, c_local, group=group)
-    return torch.stack(slabs, 0).permute(1, 0, 2).reshape(c_local.shape[0], N)
+    M = c_local.shape[0]
+    out = torch.empty((world, M, cols), dtype=c_local.dtype, device=c_local.device)
+    if dist.get_backend(group) == "nccl":
+        dist.all_gather_into_tensor(out, c_local, group=group)  # straight into the slabs
+    else:  # backends without the flat form (gloo, the CPU tests): one slab view per rank
+        dist.all_gather(list(out.unbind(0)), c_local, group=group)
+    if layout == "slabs":
+        return out
+    return out.permute(1, 0, 2).reshape(M, N)
+
+
+def n_sharded_allgather_panels(local_gemm_rows: Callable[[int, int], torch.Tensor], M: int, N: int, world: int,
+                               rank: int, panels: int = 4, group=None) -> torch.Tensor:
+    """Column-parallel GEMM whose output all-gather overlaps the GEMM itself.
+
+    The rank's GEMM runs in `panels` row panels (local_gemm_rows(row0, rows) ->
+    this rank's columns of C rows [row0, row0 + rows), [rows, N / world]); each
+    panel's all-gather is started asynchronously as soon as the panel is computed
+    and runs on the collective's own stream while the next panel's GEMM runs.
+    Returns C in the slab layout [world, M, N / world] (see n_sharded_allgather),
+    complete once the call returns (the current stream waits for every gather)."""
+    col0, cols = col_range(N, world, rank)
+    assert N % (128 * world) == 0, "N-shard needs N divisible by 128 * world"
+    out = None
+    works = []
+    rows_per = -(-M // panels)
+    rows_per = -(-rows_per // 128) * 128  # panels start on 128-row tile (and scale-atom) boundaries
+    for row0 in range(0, M, rows_per):
+        rows = min(rows_per, M - row0)
+        c_p = local_gemm_rows(row0, rows).contiguous()
+        if out is None:
+            out = torch.empty((world, M, cols), dtype=c_p.dtype, device=c_p.device)
+        # slab g's rows [row0, row0 + rows) are contiguous, so every rank's piece lands in place
+        works.append(dist.all_gather([out[g, row0:row0 + rows] for g in range(world)], c_p, group=group,
+                                     async_op=True))
+    for w in works:
+        w.wait()
+    return out
 
 
 def peer_output(M: int, N: int, dtype: torch.dtype, group=None) -> tuple[torch.Tensor, list[int]]:

@@ -62,6 +62,19 @@ def _rank_main(rank: int, world: int, port: int) -> None:
             gathered = shard.n_sharded_allgather(local, N, world, rank)
             torch.cuda.synchronize()
             assert torch.equal(gathered, ref), (M, N, K, dtype, rank, "allgather")
+            # slab layout [world, M, N / world], and gathered panel by panel under the GEMM
+            slabs = shard.n_sharded_allgather(local, N, world, rank, layout="slabs")
+            slab_ref = torch.stack([ref[:, g * cols:(g + 1) * cols] for g in range(world)])
+            torch.cuda.synchronize()
+            assert torch.equal(slabs, slab_ref), (M, N, K, dtype, rank, "slabs")
+            if M % 128 == 0:
+                def local_rows(r0, nr):
+                    return ops.mxfp8_gemm(qa[r0:r0 + nr], qb_l,
+                                          sfa[shard.sf_tc_row_offset(r0, K):shard.sf_tc_row_offset(r0 + nr, K)],
+                                          sfb_l, out_dtype=dtype)
+                panels = shard.n_sharded_allgather_panels(local_rows, M, N, world, rank, panels=3)
+                torch.cuda.synchronize()
+                assert torch.equal(panels, slab_ref), (M, N, K, dtype, rank, "panels")
             assert ops.device_status() == 0
             dist.barrier()
             del c_full

@@ -1,5 +1,6 @@
 """Multi-GPU partitioning logic on CPU ranks (gloo, world size 2): the M-shard row
-ranges and the N-shard all-gather reassemble the full product.  The local GEMM
+ranges and the N-shard all-gathers (assembled [M, N], slab layout, and panel by
+panel) reassemble the full product.  The local GEMM
 is the oracle here (a CPU stand-in injected by the test); on GPUs it is the
 library's kernel."""
 import os
@@ -53,10 +54,19 @@ def _worker(rank, world, port, M, N, K, out_dir):
     def local_cols(col0, cols):  # N-shard: this rank's columns, A replicated
         return torch.from_numpy(O.gemm_mx(qa, qb[col0:col0 + cols], sa, sb[col0:col0 + cols], M, cols, K))
 
+    def local_rows_cols(row0, rows):  # N-shard by row panels: this rank's columns of rows [row0, row0 + rows)
+        col0, cols = shard.col_range(N, world, rank)
+        return torch.from_numpy(O.gemm_mx(qa[row0:row0 + rows], qb[col0:col0 + cols], sa[row0:row0 + rows],
+                                          sb[col0:col0 + cols], rows, cols, K))
+
     part = shard.m_sharded(local_rows, M, world, rank)
     gathered = shard.n_sharded_allgather(local_cols, N, world, rank)
+    slabs = shard.n_sharded_allgather(local_cols, N, world, rank, layout="slabs")
+    panels = shard.n_sharded_allgather_panels(local_rows_cols, M, N, world, rank, panels=3)
     np.save(os.path.join(out_dir, f"m{rank}.npy"), part.numpy())
     np.save(os.path.join(out_dir, f"n{rank}.npy"), gathered.numpy())
+    np.save(os.path.join(out_dir, f"s{rank}.npy"), slabs.numpy())
+    np.save(os.path.join(out_dir, f"p{rank}.npy"), panels.numpy())
     dist.barrier()
     dist.destroy_process_group()
 
@@ -70,5 +80,9 @@ def test_m_and_n_shard_gloo_world2(tmp_path, oracle):
     full = oracle.gemm_mx(qa, qb, sa, sb, M, N, K)
     m_parts = np.concatenate([np.load(tmp_path / f"m{r}.npy") for r in range(world)], 0)
     assert np.array_equal(m_parts, full)
+    cols = N // world
+    slab_ref = np.stack([full[:, g * cols:(g + 1) * cols] for g in range(world)])
     for r in range(world):
         assert np.array_equal(np.load(tmp_path / f"n{r}.npy"), full)
+        assert np.array_equal(np.load(tmp_path / f"s{r}.npy"), slab_ref)
+        assert np.array_equal(np.load(tmp_path / f"p{r}.npy"), slab_ref)
