@@ -525,6 +525,25 @@ long long sf_row_block_bytes(const Req& r) {
   return static_cast<long long>(cdiv(r.K, 128)) * 512 * (r.mode == kModeMX4 ? 2 : 1);
 }
 
+// Blockwise GEMMs with 32 < M <= 128 and a long K run the blockwise decode kernel
+// untransposed (rows of A on the MMA's M): every SM streams an equal share of B
+// (stream-K) instead of the single-CTA kernel's one CTA per 128-column tile.  Its
+// per-call cost (about 3 us of prologue and the split-tile fix-up) only pays back
+// over enough K blocks.  Measured on B200 (graph replay, L2 flushed; M = 64 / 100 /
+// 128, N = 4096..28672): with 128 x 128 weight scales it wins from K/128 = 56 on
+// (K = 7168: 25.7 against 26.8 us; K = 18432: 45.9 against 64.0 us) and loses at
+// K <= 4096 (K = 2048: 19.6 against 11.2 us); with per-column scales it wins from
+// K/128 = 32 (K = 18432: 54.9 against 128.7 us, 128 x 28672 x 4096: 48 against
+// 64 us).  B2G_BLK_NT=0 / 1 forces either route (read at every call).
+bool skinny_blk_nt(const Req& r) {
+  if (r.mode != kModeBlk || r.M > 128 || r.batch != 1) return false;
+  const char* v = getenv("B2G_BLK_NT");
+  if (v && v[0] == '0') return false;
+  if (v && v[0] == '1') return r.M > 16;
+  const int kb = r.K / 128;
+  return r.M > 32 && (kb >= 48 || (r.group_n == 1 && kb >= 32));
+}
+
 // Few rows of A (decode): the transposed stream-K kernel.
 bool use_skinny(const Req& r, int sms) {
   static const bool off = [] {
@@ -537,9 +556,11 @@ bool use_skinny(const Req& r, int sms) {
   // only for at most 32 rows of A and more 128-row tiles than SMs (the single-CTA
   // kernel then needs a second, partial wave).  It TMA-loads the scale rows, which
   // must start on 16 bytes.
-  if (r.mode == kModeBlk)
-    return r.M <= 32 && cdiv(r.N, 128) > sms && r.stride_sfa % 4 == 0 && aligned16(r.bsa) &&
-           (r.group_n == 1 || (r.stride_sfb % 4 == 0 && aligned16(r.bsb)));
+  if (r.mode == kModeBlk) {
+    const bool scales_ok = r.stride_sfa % 4 == 0 && aligned16(r.bsa) &&
+                           (r.group_n == 1 || (r.stride_sfb % 4 == 0 && aligned16(r.bsb)));
+    return scales_ok && ((r.M <= 32 && cdiv(r.N, 128) > sms) || skinny_blk_nt(r));
+  }
   return true;
 }
 
@@ -553,11 +574,13 @@ bool use_pdl() {
 }
 
 int skinny_mp(int M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128; }
+// rows of A per stage of a decode launch: M rounded up, or all 128 MMA rows untransposed
+int skinny_rows(const Req& r) { return skinny_blk_nt(r) ? 128 : skinny_mp(r.M); }
 
 
 // 128-K blocks per ring stage: two (one 32 KB request of B) when K splits into
 // whole pairs of blocks and the stage still leaves room for a deep ring.
-int skinny_kkb(const Req& r) { return (r.K % 256 == 0 && skinny_mp(r.M) <= 64) ? 2 : 1; }
+int skinny_kkb(const Req& r) { return (r.K % 256 == 0 && skinny_rows(r) <= 64) ? 2 : 1; }
 
 long long skinny_units(const Req& r) {
   return static_cast<long long>(cdiv(r.N, 128)) * (cdiv(r.K, 128) / skinny_kkb(r));
@@ -600,7 +623,7 @@ int skinny_grid(const Req& r, int sms, int NT, int KG) {
 size_t split_ws_bytes(const Req& r, int S, int sms) {
   if (use_skinny(r, sms)) {  // fp32 partial slots, two per CTA
     const long long grid = std::min<long long>(skinny_units(r), sms);
-    return static_cast<size_t>(2 * grid) * skinny_mp(r.M) * 128 * 4;
+    return static_cast<size_t>(2 * grid) * skinny_rows(r) * 128 * 4;
   }
   // fp32 output adds its split-K partials into C in place, unless the epilogue has
   // beta * C or bias terms: those go through the workspace and the reduce
@@ -649,9 +672,10 @@ int launch_skinny_blk(const Env& d, const CUtensorMap& tw, const CUtensorMap& ta
   return B2G_OK;
 }
 
-int dispatch_skinny_blk(const Env& d, int mp, int kkb, const CUtensorMap& tw, const CUtensorMap& ta,
+int dispatch_skinny_blk(const Env& d, int mp, int kkb, bool nt, const CUtensorMap& tw, const CUtensorMap& ta,
                         const CUtensorMap& tsa, const CUtensorMap& tsb, const SkinnyParams& sp, int grid,
                         cudaStream_t st) {
+  if (nt) return launch_skinny_blk<SkinnyBlkCfg<128, 1, true>>(d, tw, ta, tsa, tsb, sp, grid, st);
   if (kkb == 2) {
     switch (mp) {
       case 16: return launch_skinny_blk<SkinnyBlkCfg<16, 2>>(d, tw, ta, tsa, tsb, sp, grid, st);
@@ -689,7 +713,7 @@ std::atomic<unsigned long long> g_skinny_tag{0};
 
 int run_skinny(const Req& r, const Env& d) {
   int rc = B2G_OK;
-  const int mp = skinny_mp(r.M);
+  const int mp = skinny_rows(r);
   const int kkb = skinny_kkb(r);
   SkinnyParams sp;
   memset(&sp, 0, sizeof(sp));
@@ -791,7 +815,7 @@ int run_skinny(const Req& r, const Env& d) {
       rc = encode(&tsb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, r.bsb, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
     }
     if (rc) return rc;
-    rc = dispatch_skinny_blk(d, mp, kkb, tw, ta, tsa, tsb, sp, grid, r.stream);
+    rc = dispatch_skinny_blk(d, mp, kkb, skinny_blk_nt(r), tw, ta, tsa, tsb, sp, grid, r.stream);
   }
   else if (r.mode == kModeMX)
     rc = r.bpre ? dispatch_skinny_mp<kModeMX, true>(d, mp, kkb, tw, ta, sp, grid, r.stream)

@@ -114,20 +114,23 @@ __device__ __forceinline__ int skinny_slot(int c, int nt, long long U, int G, in
   return 2 * c + (lo / KG == nt ? 0 : 1);
 }
 
-// The four epilogue warps (128 threads) synchronise on named barrier 1.
-__device__ __forceinline__ void skinny_epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// The epilogue warps (kEpiThreads threads: 128, or 256 in the untransposed
+// blockwise kernel) synchronise on named barrier 1.
+template <int kEpiThreads = 128>
+__device__ __forceinline__ void skinny_epi_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kEpiThreads) : "memory"); }
 
 // True on every epilogue thread iff `ok` holds on all of them, so the warps
 // leave their loop together and never strand one another at a barrier.
+template <int kEpiThreads = 128>
 __device__ __forceinline__ bool skinny_epi_all(bool ok) {
   uint32_t r;
   asm volatile(
       "{\n\t.reg .pred p, q;\n\t"
       "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.and.pred q, 1, 128, p;\n\t"
+      "bar.red.and.pred q, 1, %2, p;\n\t"
       "selp.u32 %0, 1, 0, q;\n\t}"
       : "=r"(r)
-      : "r"(static_cast<uint32_t>(ok))
+      : "r"(static_cast<uint32_t>(ok)), "n"(kEpiThreads)
       : "memory");
   return r != 0;
 }

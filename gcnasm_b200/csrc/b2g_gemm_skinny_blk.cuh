@@ -24,11 +24,25 @@
 
 namespace b2g {
 
-template <int kMP_, int kKB_>
+// kNT ("not transposed"): the MMA's M = 128 runs over the rows of A (MP = 128, rows
+// past M read as zero) and its N = 128 over the tile's weight rows, so a TMEM lane
+// is a row of C and a column a column of C.  With 128 x 128 weight scales the
+// promotion then needs one scale product per thread and K block (sfa of its row
+// times the tile's block scale) instead of one per column; C rows are written by
+// their own thread and the split-tile pieces are row-major.
+template <int kMP_, int kKB_, bool kNT_ = false>
 struct SkinnyBlkCfg {
-  static constexpr int kMP = kMP_;  // padded A rows = MMA N
+  static constexpr bool kNT = kNT_;
+  static constexpr int kMP = kMP_;  // padded A rows = MMA N (kNT: MMA M)
   static constexpr int kKB = kKB_;  // 128-K blocks per stage
-  static constexpr int kThreads = 192;  // producer, MMA, 4 epilogue warps
+  // producer, MMA, then 4 epilogue warps (one per TMEM lane group).  Untransposed:
+  // 12 warps -- warpgroup 0 (producer, MMA issuer, two idle warps) at 56 registers
+  // and 8 epilogue warps, two per lane group, each folding 64 of the tile's 128
+  // columns, at 224 (setmaxnreg; 128 * 56 + 256 * 224 = 384 * 168, the launch's total)
+  static constexpr int kEpiThreads = kNT_ ? 256 : 128;
+  static constexpr int kFirstEpiWarp = kNT_ ? 4 : 2;
+  static constexpr int kThreads = 32 * kFirstEpiWarp + kEpiThreads;
+  static constexpr int kNAcc = kNT_ ? 64 : kMP_;  // fp32 sums per epilogue thread
   static constexpr int kWBlk = 128 * 128;
   static constexpr int kABlk = kMP * 128;
   static constexpr int kWBytes = kKB * kWBlk;
@@ -63,6 +77,7 @@ struct SkinnyBlkCfg {
   static_assert(kStages * kKB <= kScaleDepth, "the first ring fill needs no free scale slot");
   static_assert(kOffScale % 128 == 0 && (kScaleSlot * 4) % 128 == 0 && (kSaFloats * 4) % 128 == 0,
                 "every scale TMA box lands on a 128-byte boundary");
+  static_assert(!kNT || (kMP == 128 && kKB == 1), "the untransposed form takes 128 A rows, one K block per stage");
 };
 
 template <class Cfg>
@@ -135,8 +150,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
   const int pre = static_cast<int>(u_hi - u_lo < ST ? u_hi - u_lo : ST);
   if (threadIdx.x == 0) {
     for (int s = 0; s < ST; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-    for (int s = 0; s < AS; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], 4); }
-    for (int s = 0; s < SD; ++s) { mbar_init(&sfull[s], 1); mbar_init(&sempty[s], 4); }
+    constexpr int kEpiWarps = Cfg::kEpiThreads / 32;
+    for (int s = 0; s < AS; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], kEpiWarps); }
+    for (int s = 0; s < SD; ++s) { mbar_init(&sfull[s], 1); mbar_init(&sempty[s], kEpiWarps); }
     mbar_init(fin, 1);
     mbar_init(never, 1);
     *abort_flag = 0;
@@ -158,6 +174,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
+    if constexpr (Cfg::kNT) setmaxnreg_dec<56>();
     if (lane == 0) {
       int s = pre % ST;
       uint32_t ph = pre == ST ? 1u : 0u;
@@ -183,6 +200,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer: one TMEM buffer per K block
+    if constexpr (Cfg::kNT) setmaxnreg_dec<56>();
     if (lane == 0) {
       int s = 0, as = 0;
       uint32_t ph = 0, aph = 0;
@@ -199,9 +217,14 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
           const uint32_t a_base = smem_u32(smem + Cfg::kOffA + s * Cfg::kABytes + j * Cfg::kABlk);
           const uint32_t d_tmem = tmem_base + as * Cfg::kAccStride;
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_f8f6f4(d_tmem, desc_kmajor_sw128(w_base + kk * 32), desc_kmajor_sw128(a_base + kk * 32),
-                       idesc_f8f6f4(128, MP), kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < 4; ++kk) {
+            if constexpr (Cfg::kNT)  // rows of A x weight rows
+              mma_f8f6f4(d_tmem, desc_kmajor_sw128(a_base + kk * 32), desc_kmajor_sw128(w_base + kk * 32),
+                         idesc_f8f6f4(128, 128), kk > 0 ? 1u : 0u);
+            else  // weight rows x rows of A
+              mma_f8f6f4(d_tmem, desc_kmajor_sw128(w_base + kk * 32), desc_kmajor_sw128(a_base + kk * 32),
+                         idesc_f8f6f4(128, MP), kk > 0 ? 1u : 0u);
+          }
           tc_commit(&acc_full[as]);
           if (++as == AS) { as = 0; aph ^= 1; }
         }
@@ -214,12 +237,18 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       mbar_wait(fin, 0, &no_abort, p.status, kDevTimeoutDrain, 1000000000ull);
     }
     __syncwarp();
+  } else if (warp < Cfg::kFirstEpiWarp) {
+    // ------------------------------------------------------------ idle (kNT: the rest of warpgroup 0)
+    if constexpr (Cfg::kNT) setmaxnreg_dec<56>();
   } else {
     // ------------------------------------------------------------ epilogue: 4 warps, one TMEM lane group each
+    if constexpr (Cfg::kNT) setmaxnreg_inc<224>();
     constexpr int CH = MP < 32 ? MP : 32;
     const int quad = warp & 3;
-    const int r = quad * 32 + lane;  // TMEM lane = weight row in the tile = output column in the tile
-    const int et = threadIdx.x - 64;
+    // TMEM lane: a weight row of the tile = a column of C (kNT: a row of A = a row of C)
+    const int r = quad * 32 + lane;
+    const int ch0 = Cfg::kNT ? ((warp - Cfg::kFirstEpiWarp) >> 2) * Cfg::kNAcc : 0;  // kNT: first column
+    const int et = threadIdx.x - 32 * Cfg::kFirstEpiWarp;
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
     const int cta = static_cast<int>(blockIdx.x);
     int as = 0;
@@ -237,15 +266,18 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       const bool fin_seg = seg_end == u_hi;
       unsigned long long* cnt = p.cnt + nt;
       const unsigned long long all_others = (p.tag << 16) | static_cast<unsigned long long>(nseg - 1);
-      auto piece = [&](int jj) {
-        return p.part + static_cast<long long>(skinny_slot(c0 + jj, nt, U, G, p.KG)) * MP * 128 + r;
+      auto slot_base = [&](int jj) {
+        return p.part + static_cast<long long>(skinny_slot(c0 + jj, nt, U, G, p.KG)) * MP * 128;
       };
-      if (nseg > 1 && fin_seg && et < nseg && et != j) bulk_prefetch_l2(piece(et) - r, MP * 128 * 4);
+      // this thread's part of piece jj: column r, stride 128 per row of A (kNT: row r of a
+      // column-major piece, stride 128 per column, so a warp's 32 rows are one 128-byte run)
+      auto piece = [&](int jj) { return slot_base(jj) + (Cfg::kNT ? ch0 * 128 + r : r); };
+      if (nseg > 1 && fin_seg && et < nseg && et != j) bulk_prefetch_l2(slot_base(et), MP * 128 * 4);
 
       // ---- fold the segment's K blocks into registers
-      float acc[MP];
+      float acc[Cfg::kNAcc];
 #pragma unroll
-      for (int m = 0; m < MP; ++m) acc[m] = 0.f;
+      for (int m = 0; m < Cfg::kNAcc; ++m) acc[m] = 0.f;
       const long long q_end = q + (seg_end - u) * KBS;
       int kb = static_cast<int>(u - t0) * KBS;  // K block within the tile
       for (; q < q_end; ++q, ++kb) {
@@ -254,10 +286,28 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         bool got = mbar_wait(&sfull[sslot], static_cast<uint32_t>(q / SD) & 1u, abort_flag, p.status,
                              kDevTimeoutEpilogue, tmo);
         got = got && mbar_wait(&acc_full[as], aph, abort_flag, p.status, kDevTimeoutEpilogue, tmo);
-        if (!skinny_epi_all(got)) { ok = false; break; }
+        if (!skinny_epi_all<Cfg::kEpiThreads>(got)) { ok = false; break; }
         const float sbc = gn1 ? slot[Cfg::kSaFloats + r] : slot[Cfg::kSaFloats + (kb & 3)];
         tc_fence_after();
         const uint32_t acc_addr = tmem_base + lane_addr + as * Cfg::kAccStride;
+        if constexpr (Cfg::kNT) {  // row r of the tile: scale sfa[r] (x the block scale, or the column's)
+          const float sar = slot[r];
+          const float s_row = sar * slot[Cfg::kSaFloats + (kb & 3)];
+#pragma unroll
+          for (int mc = 0; mc < Cfg::kNAcc; mc += 32) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(acc_addr + ch0 + mc, v);
+            tc_wait_ld();
+            if (gn1) {  // (P * sfb[n]) * sfa[m] + acc
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                acc[mc + i] = fmaf(__uint_as_float(v[i]) * slot[Cfg::kSaFloats + ch0 + mc + i], sar, acc[mc + i]);
+            } else {    // P * (sfa[m] * sfb) + acc
+#pragma unroll
+              for (int i = 0; i < 32; ++i) acc[mc + i] = fmaf(__uint_as_float(v[i]), s_row, acc[mc + i]);
+            }
+          }
+        } else {
 #pragma unroll
         for (int mc = 0; mc < MP; mc += CH) {
           uint32_t v[CH];
@@ -276,6 +326,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
               acc[mc + i] = fmaf(__uint_as_float(v[i]), slot[mc + i] * sbc, acc[mc + i]);
           }
         }
+        }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
@@ -289,6 +340,29 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       // ---- complete the tile: direct store, or the skinny kernel's right fold of the pieces
       const int n = nt * 128 + r;
       const bool col_ok = n < p.N;
+      // kNT: columns [mc, mc + 32) of row r of the tile, 16-byte stores (N and the row
+      // pitch are whole 16 bytes, so a 4- or 8-column group is all in or all out)
+      auto store_row = [&](int mc, const float (&x)[32]) {
+        if (r >= p.M) return;
+        const int n0 = nt * 128 + ch0 + mc;
+        if (p.out_f32) {
+          float* row = static_cast<float*>(p.out) + static_cast<long long>(r) * p.ldo + n0;
+#pragma unroll
+          for (int i = 0; i < 32; i += 4)
+            if (n0 + i < p.N)
+              st_global_v4(row + i, __float_as_uint(x[i] * p.alpha), __float_as_uint(x[i + 1] * p.alpha),
+                           __float_as_uint(x[i + 2] * p.alpha), __float_as_uint(x[i + 3] * p.alpha));
+        } else {
+          __nv_bfloat16* row = static_cast<__nv_bfloat16*>(p.out) + static_cast<long long>(r) * p.ldo + n0;
+#pragma unroll
+          for (int i = 0; i < 32; i += 8)
+            if (n0 + i < p.N)
+              st_global_v4(row + i, pack_bf16x2(x[i] * p.alpha, x[i + 1] * p.alpha),
+                           pack_bf16x2(x[i + 2] * p.alpha, x[i + 3] * p.alpha),
+                           pack_bf16x2(x[i + 4] * p.alpha, x[i + 5] * p.alpha),
+                           pack_bf16x2(x[i + 6] * p.alpha, x[i + 7] * p.alpha));
+        }
+      };
       auto store_out = [&](int mc, const float (&x)[CH]) {
         if (!col_ok) return;
         if (p.out_f32) {
@@ -304,26 +378,42 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         }
       };
       if (nseg == 1) {
+        if constexpr (Cfg::kNT) {
 #pragma unroll
-        for (int mc = 0; mc < MP; mc += CH) {
-          float x[CH];
+          for (int mc = 0; mc < Cfg::kNAcc; mc += 32) {
+            float x[32];
 #pragma unroll
-          for (int i = 0; i < CH; ++i) x[i] = acc[mc + i];
-          store_out(mc, x);
+            for (int i = 0; i < 32; ++i) x[i] = acc[mc + i];
+            store_row(mc, x);
+          }
+        } else {
+#pragma unroll
+          for (int mc = 0; mc < MP; mc += CH) {
+            float x[CH];
+#pragma unroll
+            for (int i = 0; i < CH; ++i) x[i] = acc[mc + i];
+            store_out(mc, x);
+          }
         }
       } else {
         bool last = false;
         if (fin_seg) {  // the tile's other pieces usually finished long ago
           if (et == 0) *last_flag = ld_acquire_gpu_u64(cnt) == all_others ? 1u : 0u;
-          skinny_epi_bar();
+          skinny_epi_bar<Cfg::kEpiThreads>();
           last = *last_flag != 0;
-          skinny_epi_bar();  // every thread has read the flag before it is written again
+          skinny_epi_bar<Cfg::kEpiThreads>();  // every thread has read the flag before it is written again
         }
         if (!last) {
           float* mine = piece(j);
+          if constexpr (Cfg::kNT) {
 #pragma unroll
-          for (int m = 0; m < MP; ++m) __stcg(mine + m * 128, acc[m]);
-          skinny_epi_bar();
+            for (int i = 0; i < Cfg::kNAcc; ++i)
+              if (r < p.M) __stcg(mine + i * 128, acc[i]);  // rows past M hold zeros: never read
+          } else {
+#pragma unroll
+            for (int m = 0; m < MP; ++m) __stcg(mine + m * 128, acc[m]);
+          }
+          skinny_epi_bar<Cfg::kEpiThreads>();
           if (et == 0) {
             fence_acq_rel_gpu();
             const int arrivals = skinny_arrive(cnt, p.tag, fin_seg ? nseg - 1 : 0, p.status);
@@ -331,29 +421,50 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             if (done) fence_acq_rel_gpu();
             *last_flag = done ? 1u : 0u;
           }
-          skinny_epi_bar();
+          skinny_epi_bar<Cfg::kEpiThreads>();
           last = *last_flag != 0;
-          skinny_epi_bar();
+          skinny_epi_bar<Cfg::kEpiThreads>();
         }
         if (last) {
           // p_0 + (p_1 + (... + p_{n-1})), this CTA's piece from registers
+          if constexpr (Cfg::kNT) {
 #pragma unroll
-          for (int mc = 0; mc < MP; mc += CH) {
-            float t[CH];
-            for (int jj = nseg - 1; jj >= 0; --jj) {
-              float y[CH];
-              if (jj == j) {
+            for (int mc = 0; mc < Cfg::kNAcc; mc += 32) {
+              float t[32];
+              for (int jj = nseg - 1; jj >= 0; --jj) {
+                float y[32];
+                if (jj == j) {
 #pragma unroll
-                for (int i = 0; i < CH; ++i) y[i] = acc[mc + i];
-              } else {
-                const float* pj = piece(jj) + mc * 128;
+                  for (int i = 0; i < 32; ++i) y[i] = acc[mc + i];
+                } else {
+                  const float* pj = piece(jj) + mc * 128;
 #pragma unroll
-                for (int i = 0; i < CH; ++i) y[i] = __ldcg(pj + i * 128);
+                  for (int i = 0; i < 32; ++i) y[i] = r < p.M ? __ldcg(pj + i * 128) : 0.f;
+                }
+#pragma unroll
+                for (int i = 0; i < 32; ++i) t[i] = jj == nseg - 1 ? y[i] : y[i] + t[i];
               }
-#pragma unroll
-              for (int i = 0; i < CH; ++i) t[i] = jj == nseg - 1 ? y[i] : y[i] + t[i];
+              store_row(mc, t);
             }
-            store_out(mc, t);
+          } else {
+#pragma unroll
+            for (int mc = 0; mc < MP; mc += CH) {
+              float t[CH];
+              for (int jj = nseg - 1; jj >= 0; --jj) {
+                float y[CH];
+                if (jj == j) {
+#pragma unroll
+                  for (int i = 0; i < CH; ++i) y[i] = acc[mc + i];
+                } else {
+                  const float* pj = piece(jj) + mc * 128;
+#pragma unroll
+                  for (int i = 0; i < CH; ++i) y[i] = __ldcg(pj + i * 128);
+                }
+#pragma unroll
+                for (int i = 0; i < CH; ++i) t[i] = jj == nseg - 1 ? y[i] : y[i] + t[i];
+              }
+              store_out(mc, t);
+            }
           }
           if (et == 0) *reinterpret_cast<volatile unsigned long long*>(cnt) = 0ull;
         }

@@ -783,3 +783,31 @@ def test_mxfp8_a2a_out_local_peers(dev, oracle, M, N, K, out, n_peers, self_inde
         check_out(block, ref[:, q * shard:(q + 1) * shard], od)
         rest = torch.cat([w[:self_index * M], w[(self_index + 1) * M:]])
         assert torch.isnan(rest.float()).all()
+
+
+# ------------------------------------------------------------------ blockwise, 32 < M <= 128: untransposed stream-K
+@pytest.mark.parametrize("M,N,K", [(128, 7168, 2048), (100, 1024, 4096), (64, 4096, 7168), (40, 512, 1024),
+                                   (128, 256, 128), (24, 2048, 1024)])
+@pytest.mark.parametrize("group_n", [128, 1])
+@pytest.mark.parametrize("out_dtype", ["bf16", "f32"])
+def test_blockscale_stream_k_untransposed(dev, oracle, monkeypatch, M, N, K, group_n, out_dtype):
+    """Rows of A on the MMA's M, every SM on a stream-K share of (tile, K block)
+    units, split tiles folded in the kernel (forced with B2G_BLK_NT=1, which the
+    default routing picks for long K only): ragged M, tiles cut into many pieces
+    (K=7168 over 32 tiles), few units (one tile), both weight-scale layouts."""
+    from gcnasm_b200 import ops
+    monkeypatch.setenv("B2G_BLK_NT", "1")
+    od = torch.bfloat16 if out_dtype == "bf16" else torch.float32
+    qa, sfa = oracle.quant_1x128(oracle.normal_rows(61, 0, M, K))
+    if group_n == 128:
+        qb, sfb = oracle.quant_128x128(oracle.normal_rows(62, 0, N, K))
+        ref = oracle.gemm_blockscale_f64(qa, qb, sfa, sfb, M, N, K, M, K // 128, 128, 0)
+    else:
+        qb, sfb = oracle.quant_1x128(oracle.normal_rows(62, 0, N, K))  # [K/128, N]
+        ref = oracle.gemm_blockscale_f64(qa, qb, sfa, sfb, M, N, K, M, N, 1, 1)
+    args = (T(qa, dev), T(qb, dev), T(sfa, dev), T(sfb, dev))
+    for _ in range(2):  # twice: the tile counters are back at zero after a launch
+        out = ops.gemm_a8w8_blockscale(*args, group_n=group_n, out_dtype=od)
+        torch.cuda.synchronize()
+        assert ops.device_status() == 0
+        check_out(out, ref, od)
