@@ -114,7 +114,7 @@ def cpu_gemm_sample(M, N, K, budget_s=12.0, seed=0):
     from oracle import oracle as O
 
     qb, sb = O.quant_mx(O.normal_rows(5678, 0, N, K))
-    probe = 8
+    probe = 64
     qa, sa = O.quant_mx(O.normal_rows(1234, 0, probe, K))
     t = time.perf_counter()
     O.gemm_mx(qa, qb, sa, sb, probe, N, K, acc_f64=False)
@@ -587,22 +587,33 @@ def bench_blockwise(args, dev, stream, peaks, flush):
             bound = "tensor" if flops / nbytes > ridge else "hbm"
             for gn in (128, 1):
                 qb, sfb = wq[gn]
+                if bound == "hbm":
+                    # a few tens of microseconds: calls back to back from a CUDA graph (no host cost
+                    # per call), B rotating over copies past twice the L2 as a serving loop streams a
+                    # different weight per GEMM, L2 flushed before each replay
+                    ms, method = blockwise_graph_ms(args, dev, stream, flush, qa, sfa, qb, sfb, gn, out)
+                else:
+                    def step():
+                        ops.gemm_a8w8_blockscale(qa, qb, sfa, sfb, group_n=gn, out=out, stream=stream)
 
-                def step():
-                    ops.gemm_a8w8_blockscale(qa, qb, sfa, sfb, group_n=gn, out=out, stream=stream)
-
-                step()
-                torch.cuda.synchronize()
-                ms = statistics.mean(timed_steps(step, reps, 3, flush, stream))
+                    step()
+                    torch.cuda.synchronize()
+                    ms = statistics.mean(timed_steps(step, reps, 3, flush, stream))
+                    method = f"{reps} single calls, CUDA events, L2 flushed before each"
                 tf, gbs = flops / (ms * 1e-3) / 1e12, nbytes / (ms * 1e-3) / 1e9
-                kern = ("b2g_gemm_skinny_blk_kernel" if (M <= 32 and N // 128 > 148) else
-                        f"b2g_gemm_kernel<Blk,{128 if M <= 128 else 256}>")
+                kb = K // 128
+                if M <= 32 and N // 128 > 148:
+                    kern = "b2g_gemm_skinny_blk_kernel (transposed stream-K)"
+                elif 32 < M <= 128 and (kb >= 48 or (gn == 1 and kb >= 32)):
+                    kern = "b2g_gemm_skinny_blk_kernel<SkinnyBlkCfg<128,1,NT>> (untransposed stream-K)"
+                else:
+                    kern = f"b2g_gemm_kernel<Blk,{128 if M <= 128 else 256}>"
                 out_rows.append({
                     "M": M, "N": N, "K": K, "group_n": gn, "us_per_call": round(ms * 1e3, 2),
                     "tflops": round(tf, 1), "hbm_gbs": round(gbs, 1), "algorithmic_flop": flops,
                     "algorithmic_bytes": nbytes, "bound": bound,
                     "frac": round(tf / fp8_peak if bound == "tensor" else gbs / peaks["hbm_gbs"], 4),
-                    "kernel": kern})
+                    "kernel": kern, "method": method})
             del qa, sfa, out
         del wq
         torch.cuda.empty_cache()
@@ -611,6 +622,40 @@ def bench_blockwise(args, dev, stream, peaks, flush):
             "ridge_flop_per_byte": round(ridge, 1),
             "peak_source": f"{peaks['source']}: FP8 = bf16 dense x2; HBM = copy bandwidth",
             "shapes": out_rows}
+
+
+def blockwise_graph_ms(args, dev, stream, flush, qa, sfa, qb, sfb, gn, out):
+    """Milliseconds per call of an HBM-bound block-scale GEMM replayed from a CUDA
+    graph: 8 calls back to back with B (and its scales) rotating over enough copies
+    to exceed twice the 126 MB L2; each replay bracketed by CUDA events, L2 flushed
+    before it."""
+    import torch
+
+    from gcnasm_b200 import ops
+
+    N, K = qb.shape
+    per_graph = 8
+    copies = max(2, -(-2 * (126 << 20) // (N * K)))
+    bs = [qb] + [qb.clone() for _ in range(copies - 1)]
+    sbs = [sfb] + [sfb.clone() for _ in range(copies - 1)]
+
+    def call(i, st=None):
+        ops.gemm_a8w8_blockscale(qa, bs[i % copies], sfa, sbs[i % copies], group_n=gn, out=out, stream=st)
+
+    for i in range(3 * copies):
+        call(i, stream)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(per_graph):
+            call(i)
+    g.replay()
+    torch.cuda.synchronize()
+    reps = max(args.steps // 4, 5)
+    ms = statistics.mean(timed_steps(g.replay, reps, 1, flush, stream)) / per_graph
+    del g, bs, sbs
+    return ms, (f"{per_graph} calls back to back from a CUDA graph, B rotating over {copies} copies, "
+                f"{reps} replays, L2 flushed before each")
 
 
 def bench_fp8_peak(args, dev, stream, flush):

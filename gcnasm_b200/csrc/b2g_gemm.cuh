@@ -525,6 +525,11 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         // fp32 block-scale promotion, one 128-K block at a time
 #pragma unroll
         for (int j = 0; j < NC; ++j) acc[j] = 0.f;
+        // the promotion keeps its sums as register pairs for the packed two-wide fp32
+        // FMA (one instruction per two columns, each rounded as the scalar fmaf)
+        float2 acc2[NC / 2];
+#pragma unroll
+        for (int j = 0; j < NC / 2; ++j) acc2[j] = make_float2(0.f, 0.f);
         const bool row_ok = m < p.M;
         const float* sa_ptr = p.bsa + w.b * p.bsa_bstride + m;
         constexpr bool gn1 = Cfg::kGn1;
@@ -566,20 +571,25 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
               tmem_ld_32x32b_x16(tmem_base + lane_addr + as * kBN + half * NC + c * KBLK + q * 16,
                                  *reinterpret_cast<uint32_t(*)[16]>(&v[q * 16]));
             tc_wait_ld();
-            if (gn1) {
+            if (gn1) {  // (P * sfb[n]) * sfa[m] + acc
+              const float2 sa2 = make_float2(sa, sa);
 #pragma unroll
               for (int j = 0; j < KBLK; j += 4) {
                 const float4 b4 = *reinterpret_cast<const float4*>(sb_stage + c * KBLK + j);
-                fmul_ffma2(acc[c * KBLK + j + 0], acc[c * KBLK + j + 1], __uint_as_float(v[j + 0]),
-                           __uint_as_float(v[j + 1]), b4.x, b4.y, sa);
-                fmul_ffma2(acc[c * KBLK + j + 2], acc[c * KBLK + j + 3], __uint_as_float(v[j + 2]),
-                           __uint_as_float(v[j + 3]), b4.z, b4.w, sa);
+                float2& a0 = acc2[(c * KBLK + j) / 2];
+                float2& a1 = acc2[(c * KBLK + j) / 2 + 1];
+                a0 = __ffma2_rn(__fmul2_rn(make_float2(__uint_as_float(v[j]), __uint_as_float(v[j + 1])),
+                                           make_float2(b4.x, b4.y)), sa2, a0);
+                a1 = __ffma2_rn(__fmul2_rn(make_float2(__uint_as_float(v[j + 2]), __uint_as_float(v[j + 3])),
+                                           make_float2(b4.z, b4.w)), sa2, a1);
               }
-            } else {
+            } else {    // P * (sfa[m] * sfb) + acc
+              const float2 s2 = make_float2(s_const, s_const);
 #pragma unroll
-              for (int j = 0; j < KBLK; j += 2)
-                ffma2_bcast(acc[c * KBLK + j], acc[c * KBLK + j + 1], __uint_as_float(v[j]),
-                            __uint_as_float(v[j + 1]), s_const);
+              for (int j = 0; j < KBLK; j += 2) {
+                float2& a = acc2[(c * KBLK + j) / 2];
+                a = __ffma2_rn(make_float2(__uint_as_float(v[j]), __uint_as_float(v[j + 1])), s2, a);
+              }
             }
           }
           tc_fence_before();
@@ -588,6 +598,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
           if (++as == AS) { as = 0; aph ^= 1; }
         }
         if (!ok) break;
+#pragma unroll
+        for (int j = 0; j < NC / 2; ++j) { acc[2 * j] = acc2[j].x; acc[2 * j + 1] = acc2[j].y; }
       }
 
       if constexpr (Cfg::kEpi) {

@@ -286,7 +286,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         bool got = mbar_wait(&sfull[sslot], static_cast<uint32_t>(q / SD) & 1u, abort_flag, p.status,
                              kDevTimeoutEpilogue, tmo);
         got = got && mbar_wait(&acc_full[as], aph, abort_flag, p.status, kDevTimeoutEpilogue, tmo);
-        if (!skinny_epi_all<Cfg::kEpiThreads>(got)) { ok = false; break; }
+        // each warp decides alone per K block (a wait that gives up raises the CTA's
+        // abort flag, so every other warp's next wait returns at once); the warps
+        // agree once per segment, before the fix-up's named barriers
+        if (!got) { ok = false; break; }
         const float sbc = gn1 ? slot[Cfg::kSaFloats + r] : slot[Cfg::kSaFloats + (kb & 3)];
         tc_fence_after();
         const uint32_t acc_addr = tmem_base + lane_addr + as * Cfg::kAccStride;
@@ -335,7 +338,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         }
         if (++as == AS) { as = 0; aph ^= 1; }
       }
-      if (!ok) break;
+      if (!skinny_epi_all<Cfg::kEpiThreads>(ok)) break;
 
       // ---- complete the tile: direct store, or the skinny kernel's right fold of the pieces
       const int n = nt * 128 + r;

@@ -811,3 +811,33 @@ def test_blockscale_stream_k_untransposed(dev, oracle, monkeypatch, M, N, K, gro
         torch.cuda.synchronize()
         assert ops.device_status() == 0
         check_out(out, ref, od)
+
+
+@pytest.mark.parametrize("nt", ["1", "0"])
+def test_bounded_wait_blockwise_decode_kernel(dev, oracle, monkeypatch, nt):
+    """The stall hook on the blockwise decode kernel (untransposed, and transposed at
+    M=16 over more weight tiles than SMs): the MMA issuer's wait gives up, every
+    epilogue warp leaves through its bounded waits and the per-segment agreement,
+    the status word reports it, and the next call on the context is correct."""
+    from gcnasm_b200 import capi, ops
+    monkeypatch.setenv("B2G_BLK_NT", nt)
+    L = capi.lib()
+    M, N, K = (100, 1024, 2048) if nt == "1" else (16, 160 * 128, 512)
+    qa, sfa = oracle.quant_1x128(oracle.normal_rows(71, 0, M, K))
+    qb, sfb = oracle.quant_128x128(oracle.normal_rows(72, 0, N, K))
+    args = (T(qa, dev), T(qb, dev), T(sfa, dev), T(sfb, dev))
+    assert ops.device_status(clear=True) == 0
+    L.b2g_set_wait_timeout_ms(200)
+    L.b2g_debug_force_stall(1)
+    try:
+        ops.gemm_a8w8_blockscale(*args, group_n=128, out_dtype=torch.float32)
+        st = C.c_int(0)
+        assert L.b2g_device_status(C.byref(st), 1) == capi.B2G_ERR_DEVICE_TIMEOUT and st.value != 0
+    finally:
+        L.b2g_debug_force_stall(0)
+        L.b2g_set_wait_timeout_ms(4000)
+    ref = oracle.gemm_blockscale_f64(qa, qb, sfa, sfb, M, N, K, M, K // 128, 128, 0)
+    out = ops.gemm_a8w8_blockscale(*args, group_n=128, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    check_out(out, ref, torch.float32)
