@@ -278,6 +278,8 @@ def run_b200(args, rank, world, local_rank):
     result["fp8_peak_cublas"] = fp8
     if "tflops_best" in fp8:
         result["roofline"]["frac_of_cublas_fp8"] = round(achieved / fp8["tflops_best"], 4)
+    if "mxfp8_tflops_best" in fp8:
+        result["roofline"]["frac_of_cublas_mxfp8"] = round(achieved / fp8["mxfp8_tflops_best"], 4)
     # ---------------------------------------------------------------- CPU baseline (oracle port, N=1)
     if world == 1:
         tf, rows, cores, secs = cpu_gemm_sample(M, N, K, budget_s=args.cpu_budget)
@@ -677,13 +679,29 @@ def bench_fp8_peak(args, dev, stream, flush):
         torch.cuda.synchronize()
         times = timed_steps(step, max(10, min(args.steps, 30)), 3, flush, stream)
         best = min(times)
-        del a, b
-        return {"tflops_best": round(2.0 * M * N * K / (best * 1e-3) / 1e12, 1),
-                "tflops_mean": round(2.0 * M * N * K / (statistics.mean(times) * 1e-3) / 1e12, 1),
-                "how": "torch._scaled_mm (cuBLAS) E4M3 8192^3 -> bf16, per-tensor scales, CUDA events, "
-                       "L2 flushed between calls"}
+        res = {"tflops_best": round(2.0 * M * N * K / (best * 1e-3) / 1e12, 1),
+               "tflops_mean": round(2.0 * M * N * K / (statistics.mean(times) * 1e-3) / 1e12, 1),
+               "how": "torch._scaled_mm (cuBLAS) E4M3 8192^3 -> bf16, per-tensor scales, CUDA events, "
+                      "L2 flushed between calls"}
     except Exception as e:  # an unsupported build leaves the derived peak as the only one
         return {"error": f"{type(e).__name__}: {e}"[:300]}
+    # the same with 1x32 UE8M0 block scales (cuBLAS's MXFP8 GEMM), the headline kernel's own format
+    try:
+        sa = torch.full((M, K // 32), 127, dtype=torch.uint8, device=dev).view(torch.float8_e8m0fnu)
+        sb = torch.full((N, K // 32), 127, dtype=torch.uint8, device=dev).view(torch.float8_e8m0fnu)
+
+        def step_mx():
+            torch._scaled_mm(a, b.t(), scale_a=sa, scale_b=sb, out_dtype=torch.bfloat16)
+
+        step_mx()
+        torch.cuda.synchronize()
+        tmx = timed_steps(step_mx, max(10, min(args.steps, 30)), 3, flush, stream)
+        res["mxfp8_tflops_best"] = round(2.0 * M * N * K / (min(tmx) * 1e-3) / 1e12, 1)
+        res["mxfp8_how"] = "torch._scaled_mm (cuBLAS) E4M3 8192^3 with 1x32 UE8M0 scales -> bf16"
+    except Exception as e:
+        res["mxfp8_error"] = f"{type(e).__name__}: {e}"[:300]
+    del a, b
+    return res
 
 
 def bench_e2e(args, dev, stream, qa, sfa_rm, qb, sfb_rm, M, N, K):
