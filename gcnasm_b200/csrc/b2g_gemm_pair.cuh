@@ -15,9 +15,15 @@
 //     into their own smem whose completion is counted on the LEADER's `full`
 //     barrier (cp.async.bulk.tensor ... .cta_group::2); the leader arms it with
 //     the bytes of both CTAs;
-//   * the leader's single MMA thread issues the MMAs (and, for MX, the
-//     tcgen05.cp of both CTAs' scale atoms) and commits with a multicast arrival
-//     on both CTAs' `empty` / `acc_full` barriers;
+//   * the leader's single MMA thread issues the MMAs and commits with a
+//     multicast arrival on both CTAs' `empty` / `acc_full` barriers;
+//   * for the MX kinds a second leader thread (the scale warp) issues the
+//     tcgen05.cp of both CTAs' scale atoms into one of kSfSets TMEM column sets
+//     and commits to `sf_full[set]`; it refills a set only after the `empty`
+//     arrival of the block that last read it.  Issuing the copies from the MMA
+//     thread stalled it: a barrier wait placed after tcgen05.cp waits for the
+//     copies to finish, which holds the issuer to one block ahead of the tensor
+//     pipe (measured: 634 instead of 512 clocks per 128-K block);
 //   * both CTAs' epilogues drain their own TMEM and arrive on the leader's
 //     `acc_empty` (16 arrivals: 8 warps x 2 CTAs).
 // Every TMA load targets its own CTA's shared memory (none is broadcast to the
@@ -37,8 +43,9 @@ struct PairCfg {
   static constexpr int kBN = kBN_;        // pair tile N (MMA N): 256 or 192
   static constexpr int kHalf = 128;       // rows of A per CTA
   static constexpr int kHalfB = kBN / 2;  // rows of B per CTA
-  static constexpr int kThreads = 320;
   static constexpr int kEpiWarps = 8;
+  static constexpr int kSfWarp = 2 + kEpiWarps;                  // MX kinds: the scale-copy warp
+  static constexpr int kThreads = 32 * (kSfWarp + (mode_mx(kMode) ? 1 : 0));
   static constexpr int kColsPerThread = kBN / 2;
 
   static constexpr int kABytes = kHalf * 128;
@@ -54,17 +61,16 @@ struct PairCfg {
   static constexpr int kStages = kMode == kModeMX4 ? 5 : 6;  // MXFP4's larger scale stages leave room for 5
   static constexpr uint32_t kTxPerStage = 2u * kStageBytes;  // both CTAs complete on the leader's barrier
 
-  // Scale factors live in TMEM in two alternating column sets: the copies for
-  // 128-K block k+1 then never overwrite columns the MMAs of block k still read.
-  // Per column set: A K-atom q at + 4q, then B K-atom q of row block j at
-  // + 4 * (q * kSfbAtoms + j).
+  // Scale factors live in TMEM in kSfSets column sets, one per 128-K block in
+  // flight (block k uses set k % kSfSets): A K-atom q at + 4q, then B K-atom q
+  // of row block j at + 4 * kKAtoms + 4 * (q * kSfbAtoms + j).
   static constexpr int kSfCols = 4 * kKAtoms * (1 + kSfbAtoms);
-  static constexpr int kSfBufs = 2;
-  static constexpr int kAccStages = (2 * kBN + kSfBufs * kSfCols <= 512) ? 2 : 1;
-  static constexpr int kSfaCol = kAccStages * kBN;  // + buffer * kSfCols
-  static constexpr int kSfbCol = kSfaCol + 4 * kKAtoms;
+  static constexpr int kSfSets = 4;
+  static constexpr int kAccStages = (2 * kBN + kSfSets * kSfCols <= 512) ? 2 : 1;
+  static constexpr int kSfCol0 = kAccStages * kBN;  // + set * kSfCols
   static constexpr int kTmemCols = 512;
-
+  static_assert(kSfCol0 + kSfSets * kSfCols <= kTmemCols, "TMEM columns: accumulators + scale sets");
+  static_assert(kSfSets <= kStages, "a scale set is refilled only after the block kSfSets back retired");
   static constexpr int kOffA = 0;
   static constexpr int kOffB = kOffA + kStages * kABytes;
   static constexpr int kOffSfa = kOffB + kStages * kBBytes;
@@ -72,7 +78,7 @@ struct PairCfg {
   static constexpr int kOffStageC = (kOffSfb + kStages * kSfbBytes + 1023) / 1024 * 1024;  // TMA-store staging
   static constexpr int kStageCBytes = kEpiWarps * 2048;                                        // 2 KB per warp
   static constexpr int kOffBar = (kOffStageC + kStageCBytes + 7) / 8 * 8;
-  static constexpr int kNumBars = 2 * kStages + 2 * kAccStages + 2;
+  static constexpr int kNumBars = 2 * kStages + 2 * kAccStages + 2 + kSfSets + 1;
   static constexpr int kOffCtl = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffCtl + 16 + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
@@ -107,6 +113,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
   uint64_t* acc_empty = bars + 2 * ST + AS;
   uint64_t* fin = bars + 2 * ST + 2 * AS;
   uint64_t* never = fin + 1;
+  uint64_t* sf_full = never + 1;  // [kSfSets]
+  uint64_t* sf_fin = sf_full + Cfg::kSfSets;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + Cfg::kOffCtl);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kOffCtl + 4);
 
@@ -121,6 +129,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     for (int s = 0; s < AS; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], 2 * Cfg::kEpiWarps); }
     mbar_init(fin, 1);
     mbar_init(never, 1);
+    for (int i = 0; i < Cfg::kSfSets; ++i) mbar_init(&sf_full[i], 1);
+    mbar_init(sf_fin, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -184,7 +194,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     // ------------------------------------------------------------ MMA issuer (leader only)
     if (leader && lane == 0) {
       int s = 0, as = 0;
-      uint32_t ph = 0, aph = 0, sfbuf = 0;
+      uint32_t ph = 0, aph = 0, kblk = 0;  // kblk: 128-K blocks issued by this pair (scale set kblk % kSfSets)
       bool ok = true;
       constexpr uint16_t kBoth = 0x3;
       if (p.debug_stall) ok = mbar_wait(never, 0, abort_flag, p.status, kDevTimeoutMma, tmo);
@@ -192,29 +202,22 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         const Unit w = decode_unit(u, p);
         if (!mbar_wait(&acc_empty[as], aph ^ 1, abort_flag, p.status, kDevTimeoutMma, tmo)) { ok = false; break; }
         tc_fence_after();
-        for (int kb = w.kb0; kb < w.kb1; ++kb) {
+        const uint32_t d_tmem = tmem_base + as * kBN;
+        // B scales of tile row 0 sit ((nt * BN) % 128) / 32 TMEM columns into the first atom
+        const uint32_t sfb_shift = ((w.nt * kBN) & 127) >> 5;
+        for (int kb = w.kb0; kb < w.kb1; ++kb, ++kblk) {
           if (!mbar_wait(&full[s], ph, abort_flag, p.status, kDevTimeoutMma, tmo)) { ok = false; break; }
+          const uint32_t set = kblk % Cfg::kSfSets;
+          if (mode_mx(kMode) &&
+              !mbar_wait(&sf_full[set], (kblk / Cfg::kSfSets) & 1u, abort_flag, p.status, kDevTimeoutMma, tmo)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
           const uint32_t a_base = smem_u32(smem + Cfg::kOffA + s * Cfg::kABytes);
           const uint32_t b_base = smem_u32(smem + Cfg::kOffB + s * Cfg::kBBytes);
-          const uint32_t d_tmem = tmem_base + as * kBN;
-          const uint32_t sf_off = sfbuf * Cfg::kSfCols;
-          if (mode_mx(kMode)) {
-#pragma unroll
-            for (int q = 0; q < Cfg::kKAtoms; ++q) {
-              tc_cp_32x128b_warpx4_pair(tmem_base + Cfg::kSfaCol + sf_off + 4 * q,
-                                        desc_sf_atom(smem_u32(smem + Cfg::kOffSfa + s * Cfg::kSfaBytes + q * 512)));
-#pragma unroll
-              for (int j = 0; j < Cfg::kSfbAtoms; ++j)
-                tc_cp_32x128b_warpx4_pair(tmem_base + Cfg::kSfbCol + sf_off + 4 * (q * Cfg::kSfbAtoms + j),
-                                          desc_sf_atom(smem_u32(smem + Cfg::kOffSfb + s * Cfg::kSfbBytes +
-                                                                (j * Cfg::kKAtoms + q) * 512)));
-            }
-          }
-          // B scales of tile row 0 sit ((nt * BN) % 128) / 32 TMEM columns into the first atom
-          const uint32_t sfa_tmem = tmem_base + Cfg::kSfaCol + sf_off;
-          const uint32_t sfb_tmem = tmem_base + Cfg::kSfbCol + sf_off + (((w.nt * kBN) & 127) >> 5);
-          sfbuf ^= 1;
+          const uint32_t sfa_tmem = tmem_base + Cfg::kSfCol0 + set * Cfg::kSfCols;
+          const uint32_t sfb_tmem = sfa_tmem + 4 * Cfg::kKAtoms + sfb_shift;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint64_t adesc = desc_kmajor_sw128(a_base + kk * 32);
@@ -239,6 +242,46 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       tc_commit_pair(fin);
       volatile int no_abort = 0;
       mbar_wait(fin, 0, &no_abort, p.status, kDevTimeoutDrain, 1000000000ull);
+    }
+    __syncwarp();
+  } else if (mode_mx(kMode) && warp == Cfg::kSfWarp) {
+    // ------------------------------------------------------------ scale copies (leader only, MX kinds)
+    // Block k's scale atoms go to set k % kSfSets once its stage has landed and
+    // the MMAs of block k - kSfSets (the set's previous reader) have retired --
+    // their commit to `empty` of that block's stage says so.  The empty phase
+    // cannot have moved on further: the MMAs of block k - kSfSets + ST wait for
+    // copies this thread has not issued yet.
+    if (leader && lane == 0) {
+      int s = 0;
+      uint32_t ph = 0, kblk = 0;
+      bool ok = true;
+      for (int u = pair; u < p.num_units && ok; u += pp.num_pairs) {
+        const Unit w = decode_unit(u, p);
+        for (int kb = w.kb0; kb < w.kb1; ++kb, ++kblk) {
+          if (!mbar_wait(&full[s], ph, abort_flag, p.status, kDevTimeoutMma, tmo)) { ok = false; break; }
+          if (kblk >= static_cast<uint32_t>(Cfg::kSfSets)) {
+            const uint32_t j = kblk - Cfg::kSfSets;
+            if (!mbar_wait(&empty[j % ST], (j / ST) & 1u, abort_flag, p.status, kDevTimeoutMma, tmo)) { ok = false; break; }
+          }
+          tc_fence_after();
+          const uint32_t set_col = tmem_base + Cfg::kSfCol0 + (kblk % Cfg::kSfSets) * Cfg::kSfCols;
+#pragma unroll
+          for (int q = 0; q < Cfg::kKAtoms; ++q) {
+            tc_cp_32x128b_warpx4_pair(set_col + 4 * q,
+                                      desc_sf_atom(smem_u32(smem + Cfg::kOffSfa + s * Cfg::kSfaBytes + q * 512)));
+#pragma unroll
+            for (int j = 0; j < Cfg::kSfbAtoms; ++j)
+              tc_cp_32x128b_warpx4_pair(set_col + 4 * Cfg::kKAtoms + 4 * (q * Cfg::kSfbAtoms + j),
+                                        desc_sf_atom(smem_u32(smem + Cfg::kOffSfb + s * Cfg::kSfbBytes +
+                                                              (j * Cfg::kKAtoms + q) * 512)));
+          }
+          tc_commit_pair(&sf_full[kblk % Cfg::kSfSets]);
+          if (++s == ST) { s = 0; ph ^= 1; }
+        }
+      }
+      tc_commit_pair(sf_fin);  // every copy retired before TMEM is freed
+      volatile int no_abort = 0;
+      mbar_wait(sf_fin, 0, &no_abort, p.status, kDevTimeoutDrain, 1000000000ull);
     }
     __syncwarp();
   } else {
