@@ -418,12 +418,21 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       if (p.debug_stall) ok = mbar_wait(never, 0, abort_flag, p.status, kDevTimeoutMma, tmo);
       for (int u = blockIdx.x; u < p.num_units && ok; u += gridDim.x) {
         const Unit w = decode_unit(u, p);
+        // the MX kinds issue scale copies from this thread: poll (mbar_wait_spin)
         if (kMode != kModeBlk) {
-          if (!mbar_wait(&acc_empty[as], aph ^ 1, abort_flag, p.status, kDevTimeoutMma, tmo)) { ok = false; break; }
+          if (!(mode_mx(kMode) ? mbar_wait_spin(&acc_empty[as], aph ^ 1, abort_flag, p.status, kDevTimeoutMma, tmo)
+                               : mbar_wait(&acc_empty[as], aph ^ 1, abort_flag, p.status, kDevTimeoutMma, tmo))) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
         }
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
-          if (!mbar_wait(&full[s], ph, abort_flag, p.status, kDevTimeoutMma, tmo)) { ok = false; break; }
+          if (!(mode_mx(kMode) ? mbar_wait_spin(&full[s], ph, abort_flag, p.status, kDevTimeoutMma, tmo)
+                               : mbar_wait(&full[s], ph, abort_flag, p.status, kDevTimeoutMma, tmo))) {
+            ok = false;
+            break;
+          }
           if (kMode == kModeBlk) {
             if (!mbar_wait(&acc_empty[as], aph ^ 1, abort_flag, p.status, kDevTimeoutMma, tmo)) { ok = false; break; }
           }

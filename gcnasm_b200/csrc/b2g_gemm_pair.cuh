@@ -250,7 +250,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     // the MMAs of block k - kSfSets (the set's previous reader) have retired --
     // their commit to `empty` of that block's stage says so.  The empty phase
     // cannot have moved on further: the MMAs of block k - kSfSets + ST wait for
-    // copies this thread has not issued yet.
+    // copies this thread has not issued yet.  Waits poll (mbar_wait_spin) so
+    // that copies of several blocks can be in flight at once.
     if (leader && lane == 0) {
       int s = 0;
       uint32_t ph = 0, kblk = 0;
@@ -258,10 +259,13 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       for (int u = pair; u < p.num_units && ok; u += pp.num_pairs) {
         const Unit w = decode_unit(u, p);
         for (int kb = w.kb0; kb < w.kb1; ++kb, ++kblk) {
-          if (!mbar_wait(&full[s], ph, abort_flag, p.status, kDevTimeoutMma, tmo)) { ok = false; break; }
+          if (!mbar_wait_spin(&full[s], ph, abort_flag, p.status, kDevTimeoutMma, tmo)) { ok = false; break; }
           if (kblk >= static_cast<uint32_t>(Cfg::kSfSets)) {
             const uint32_t j = kblk - Cfg::kSfSets;
-            if (!mbar_wait(&empty[j % ST], (j / ST) & 1u, abort_flag, p.status, kDevTimeoutMma, tmo)) { ok = false; break; }
+            if (!mbar_wait_spin(&empty[j % ST], (j / ST) & 1u, abort_flag, p.status, kDevTimeoutMma, tmo)) {
+              ok = false;
+              break;
+            }
           }
           tc_fence_after();
           const uint32_t set_col = tmem_base + Cfg::kSfCol0 + (kblk % Cfg::kSfSets) * Cfg::kSfCols;

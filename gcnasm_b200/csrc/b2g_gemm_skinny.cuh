@@ -295,11 +295,20 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       long long q = 0;
       while (ok && q < nq) {
         const long long len = seg_len(q);
-        if (!mbar_wait(&acc_empty[as], aph ^ 1, abort_flag, p.status, kDevTimeoutMma, tmo)) { ok = false; break; }
+        // the MX kinds issue scale copies from this thread: poll (mbar_wait_spin)
+        if (!(mode_mx(kMode) ? mbar_wait_spin(&acc_empty[as], aph ^ 1, abort_flag, p.status, kDevTimeoutMma, tmo)
+                             : mbar_wait(&acc_empty[as], aph ^ 1, abort_flag, p.status, kDevTimeoutMma, tmo))) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + as * Cfg::kAccStride;
         for (long long v = 0; v < len; ++v) {
-          if (!mbar_wait(&full[s], ph, abort_flag, p.status, kDevTimeoutMma, tmo)) { ok = false; break; }
+          if (!(mode_mx(kMode) ? mbar_wait_spin(&full[s], ph, abort_flag, p.status, kDevTimeoutMma, tmo)
+                               : mbar_wait(&full[s], ph, abort_flag, p.status, kDevTimeoutMma, tmo))) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
 #pragma unroll
           for (int j = 0; j < KBS; ++j) {

@@ -82,6 +82,39 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// mbar_wait for a thread that issues tcgen05.cp: it polls with the
+// non-blocking test_wait.  A blocking try_wait in a thread with scale copies in
+// flight returns only once those copies have finished, even when the phase it
+// waits for completed long before (measured on B200: 634 instead of 512 clocks
+// per 128-K block of MMAs), which holds the issuing thread to one block ahead
+// of the tensor pipe.  Same bounds and status codes as mbar_wait.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                               int* status, int code, uint64_t timeout_ns) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > timeout_ns) {
+      *abort_flag = 1;
+      if (status) atomicCAS(status, 0, code);
+      return false;
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // TMA (cp.async.bulk.tensor) and plain bulk copies, global -> shared
 // ---------------------------------------------------------------------------
