@@ -17,13 +17,14 @@
 //     the bytes of both CTAs;
 //   * the leader's single MMA thread issues the MMAs and commits with a
 //     multicast arrival on both CTAs' `empty` / `acc_full` barriers;
-//   * for the MX kinds a second leader thread (the scale warp) issues the
-//     tcgen05.cp of both CTAs' scale atoms into one of kSfSets TMEM column sets
-//     and commits to `sf_full[set]`; it refills a set only after the `empty`
-//     arrival of the block that last read it.  Issuing the copies from the MMA
-//     thread stalled it: a barrier wait placed after tcgen05.cp waits for the
-//     copies to finish, which holds the issuer to one block ahead of the tensor
-//     pipe (measured: 634 instead of 512 clocks per 128-K block);
+//   * for the MX kinds the scale warp of each CTA loads its scale atoms for
+//     kSfGroup blocks at a time into a two-slot smem ring, and the leader's
+//     scale warp copies both CTAs' atoms into TMEM (tcgen05.cp) and commits to
+//     `grp_full`; the MMA thread waits on that once per group and commits to
+//     `grp_done` after the group's MMAs.  Issuing the copies from the MMA
+//     thread stalled it: a blocking barrier wait placed after tcgen05.cp waits
+//     for the copies to finish, which holds the issuer to one block ahead of
+//     the tensor pipe (measured: 634 instead of 512 clocks per 128-K block);
 //   * both CTAs' epilogues drain their own TMEM and arrive on the leader's
 //     `acc_empty` (16 arrivals: 8 warps x 2 CTAs).
 // Every TMA load targets its own CTA's shared memory (none is broadcast to the
@@ -33,6 +34,10 @@
 #include "b2g_gemm.cuh"
 
 namespace b2g {
+
+// 128-K blocks whose scale atoms one TMA box brings in (the pair kernel's MX kinds);
+// the host encodes the scale tensor maps with boxes of this many blocks.
+constexpr int kPairSfGroup = 4;
 
 template <int kMode_, int kBN_, bool kBPre_, bool kOutF32_, bool kEpi_ = false>
 struct PairCfg {
@@ -50,35 +55,45 @@ struct PairCfg {
 
   static constexpr int kABytes = kHalf * 128;
   static constexpr int kBBytes = kHalfB * 128;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = 6 - (kMode == kModeMX4 ? 1 : 0);  // MXFP4's larger scale slots leave room for 5
+  static constexpr uint32_t kTxPerStage = 2u * kStageBytes;      // both CTAs complete on the leader's barrier
+
+  // Scale atoms travel apart from the operand stages: one TMA box per operand
+  // brings the atoms of kSfGroup consecutive 128-K blocks (the atoms of one row
+  // block are contiguous along K) into one of two smem slots, well ahead of the
+  // operands.  Loading them with every stage cost two small TMA boxes per block,
+  // which held the operand ring ~20 % below its plain-FP8 rate.
   // A 192-wide tile starts 0 or 64 rows into a 128-row scale atom, so its B
   // scales span 2 atoms and the MMA's scale address is shifted by 0 or 2 TMEM
   // columns (the even shift CUTLASS's N=192 tiles use).
   static constexpr int kSfbAtoms = 2;
   static constexpr int kKAtoms = mode_atoms(kMode);  // scale K-atoms per 128-byte K block
-  static constexpr int kSfaBytes = 512 * kKAtoms;
-  static constexpr int kSfbBytes = 512 * kSfbAtoms * kKAtoms;
-  static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;
-  static constexpr int kStages = kMode == kModeMX4 ? 5 : 6;  // MXFP4's larger scale stages leave room for 5
-  static constexpr uint32_t kTxPerStage = 2u * kStageBytes;  // both CTAs complete on the leader's barrier
+  static constexpr int kSfGroup = mode_mx(kMode) ? kPairSfGroup : 1;
+  static constexpr int kSfaSlotBytes = 512 * kKAtoms * kSfGroup;  // [K-atom][512 B]
+  static constexpr int kSfbSlotBytes = 512 * kSfbAtoms * kKAtoms * kSfGroup;  // [row block][K-atom][512 B]
+  static constexpr int kSfSlotBytes = kSfaSlotBytes + kSfbSlotBytes;
+  static constexpr int kSfSlots = mode_mx(kMode) ? 2 : 0;
+  static constexpr uint32_t kSfTxPerSlot = 2u * kSfSlotBytes;
 
-  // Scale factors live in TMEM in kSfSets column sets, one per 128-K block in
-  // flight (block k uses set k % kSfSets): A K-atom q at + 4q, then B K-atom q
-  // of row block j at + 4 * kKAtoms + 4 * (q * kSfbAtoms + j).
+  // Scale factors live in TMEM in kSfSets column sets, two groups' worth (block
+  // i of group g uses set (g % 2) * kSfGroup + i): A K-atom q at + 4q, then B
+  // K-atom q of row block j at + 4 * kKAtoms + 4 * (q * kSfbAtoms + j).
   static constexpr int kSfCols = 4 * kKAtoms * (1 + kSfbAtoms);
-  static constexpr int kSfSets = 4;
+  static constexpr int kSfSets = mode_mx(kMode) ? 2 * kSfGroup : 0;
   static constexpr int kAccStages = (2 * kBN + kSfSets * kSfCols <= 512) ? 2 : 1;
   static constexpr int kSfCol0 = kAccStages * kBN;  // + set * kSfCols
   static constexpr int kTmemCols = 512;
   static_assert(kSfCol0 + kSfSets * kSfCols <= kTmemCols, "TMEM columns: accumulators + scale sets");
-  static_assert(kSfSets <= kStages, "a scale set is refilled only after the block kSfSets back retired");
   static constexpr int kOffA = 0;
   static constexpr int kOffB = kOffA + kStages * kABytes;
-  static constexpr int kOffSfa = kOffB + kStages * kBBytes;
-  static constexpr int kOffSfb = kOffSfa + kStages * kSfaBytes;
-  static constexpr int kOffStageC = (kOffSfb + kStages * kSfbBytes + 1023) / 1024 * 1024;  // TMA-store staging
+  static constexpr int kOffSf = kOffB + kStages * kBBytes;  // + slot * kSfSlotBytes: SFA atoms, then SFB atoms
+  static constexpr int kOffStageC = (kOffSf + kSfSlots * kSfSlotBytes + 1023) / 1024 * 1024;  // TMA-store staging
   static constexpr int kStageCBytes = kEpiWarps * 2048;                                        // 2 KB per warp
   static constexpr int kOffBar = (kOffStageC + kStageCBytes + 7) / 8 * 8;
-  static constexpr int kNumBars = 2 * kStages + 2 * kAccStages + 2 + kSfSets + 1;
+  // full, empty, acc_full, acc_empty, fin, never, then sf_full, sf_empty, grp_full,
+  // grp_done (two each) and sf_fin
+  static constexpr int kNumBars = 2 * kStages + 2 * kAccStages + 2 + 8 + 1;
   static constexpr int kOffCtl = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffCtl + 16 + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
@@ -113,8 +128,11 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
   uint64_t* acc_empty = bars + 2 * ST + AS;
   uint64_t* fin = bars + 2 * ST + 2 * AS;
   uint64_t* never = fin + 1;
-  uint64_t* sf_full = never + 1;  // [kSfSets]
-  uint64_t* sf_fin = sf_full + Cfg::kSfSets;
+  uint64_t* sf_full = never + 1;      // [2] scale slot landed (both CTAs' boxes, on the leader)
+  uint64_t* sf_empty = sf_full + 2;   // [2] scale slot copied out (multicast to both CTAs)
+  uint64_t* grp_full = sf_empty + 2;  // [2] a group's scales are in TMEM (leader)
+  uint64_t* grp_done = grp_full + 2;  // [2] a group's MMAs retired: its TMEM sets are free (leader)
+  uint64_t* sf_fin = grp_done + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + Cfg::kOffCtl);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kOffCtl + 4);
 
@@ -129,7 +147,12 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     for (int s = 0; s < AS; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], 2 * Cfg::kEpiWarps); }
     mbar_init(fin, 1);
     mbar_init(never, 1);
-    for (int i = 0; i < Cfg::kSfSets; ++i) mbar_init(&sf_full[i], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sf_full[i], 1);
+      mbar_init(&sf_empty[i], 1);
+      mbar_init(&grp_full[i], 1);
+      mbar_init(&grp_done[i], 1);
+    }
     mbar_init(sf_fin, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -164,13 +187,6 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             tma_load_4d_pair(smem + Cfg::kOffB + s * Cfg::kBBytes, &tm_b, bar, 0, brow / 16, kb * 8, w.b);
           else
             tma_load_3d_pair(smem + Cfg::kOffB + s * Cfg::kBBytes, &tm_b, bar, kb * 128, brow, w.b);
-          if (mode_mx(kMode)) {
-            // scale atoms: (128 words, K-atoms, row blocks) boxes of the atom-layout buffers,
-            // landing as [row block][K-atom][512 B]
-            const int ka = kb * Cfg::kKAtoms;
-            tma_load_4d_pair(smem + Cfg::kOffSfa + s * Cfg::kSfaBytes, &tm_sfa, bar, 0, ka, w.mt * 2 + rank, w.b);
-            tma_load_4d_pair(smem + Cfg::kOffSfb + s * Cfg::kSfbBytes, &tm_sfb, bar, 0, ka, (w.nt * kBN) >> 7, w.b);
-          }
           issued_mask |= 1u << s;
           issued_phase = (issued_phase & ~(1u << s)) | (ph << s);
           if (++s == ST) { s = 0; ph ^= 1; }
@@ -194,9 +210,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     // ------------------------------------------------------------ MMA issuer (leader only)
     if (leader && lane == 0) {
       int s = 0, as = 0;
-      uint32_t ph = 0, aph = 0, kblk = 0;  // kblk: 128-K blocks issued by this pair (scale set kblk % kSfSets)
+      uint32_t ph = 0, aph = 0, g = 0;  // g: scale groups issued by this pair
       bool ok = true;
       constexpr uint16_t kBoth = 0x3;
+      constexpr int G = Cfg::kSfGroup;
       if (p.debug_stall) ok = mbar_wait(never, 0, abort_flag, p.status, kDevTimeoutMma, tmo);
       for (int u = pair; u < p.num_units && ok; u += pp.num_pairs) {
         const Unit w = decode_unit(u, p);
@@ -205,35 +222,40 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         const uint32_t d_tmem = tmem_base + as * kBN;
         // B scales of tile row 0 sit ((nt * BN) % 128) / 32 TMEM columns into the first atom
         const uint32_t sfb_shift = ((w.nt * kBN) & 127) >> 5;
-        for (int kb = w.kb0; kb < w.kb1; ++kb, ++kblk) {
-          if (!mbar_wait(&full[s], ph, abort_flag, p.status, kDevTimeoutMma, tmo)) { ok = false; break; }
-          const uint32_t set = kblk % Cfg::kSfSets;
-          if (mode_mx(kMode) &&
-              !mbar_wait(&sf_full[set], (kblk / Cfg::kSfSets) & 1u, abort_flag, p.status, kDevTimeoutMma, tmo)) {
+        for (int kb = w.kb0; kb < w.kb1 && ok; kb += G, ++g) {
+          const int gs = min(G, w.kb1 - kb);
+          const uint32_t slot = g & 1u;
+          if (mode_mx(kMode) && !mbar_wait(&grp_full[slot], (g >> 1) & 1u, abort_flag, p.status, kDevTimeoutMma, tmo)) {
             ok = false;
             break;
           }
-          tc_fence_after();
-          const uint32_t a_base = smem_u32(smem + Cfg::kOffA + s * Cfg::kABytes);
-          const uint32_t b_base = smem_u32(smem + Cfg::kOffB + s * Cfg::kBBytes);
-          const uint32_t sfa_tmem = tmem_base + Cfg::kSfCol0 + set * Cfg::kSfCols;
-          const uint32_t sfb_tmem = sfa_tmem + 4 * Cfg::kKAtoms + sfb_shift;
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t adesc = desc_kmajor_sw128(a_base + kk * 32);
-            const uint64_t bdesc = Cfg::kBPre ? desc_kmajor_interleave(b_base + kk * 2 * (Cfg::kHalfB * 16), Cfg::kHalfB * 16)
-                                              : desc_kmajor_sw128(b_base + kk * 32);
-            const uint32_t acc = (kb > w.kb0 || kk > 0);
-            if (kMode == kModeMX)
-              mma_mxf8f6f4_pair(d_tmem, adesc, bdesc, idesc_mxf8f6f4(256, kBN, kk, kk), sfa_tmem, sfb_tmem, acc);
-            else if (kMode == kModeMX4)  // K-atom kk / 2, byte pair 2 * (kk % 2)
-              mma_mxf4_pair(d_tmem, adesc, bdesc, idesc_mxf4(256, kBN, (kk & 1) * 2, (kk & 1) * 2),
-                            sfa_tmem + 4 * (kk >> 1), sfb_tmem + 4 * Cfg::kSfbAtoms * (kk >> 1), acc);
-            else
-              mma_f8f6f4_pair(d_tmem, adesc, bdesc, idesc_f8f6f4(256, kBN), acc);
+          for (int i = 0; i < G; ++i) {
+            if (i >= gs) break;
+            if (!mbar_wait(&full[s], ph, abort_flag, p.status, kDevTimeoutMma, tmo)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t a_base = smem_u32(smem + Cfg::kOffA + s * Cfg::kABytes);
+            const uint32_t b_base = smem_u32(smem + Cfg::kOffB + s * Cfg::kBBytes);
+            const uint32_t sfa_tmem = tmem_base + Cfg::kSfCol0 + (slot * G + i) * Cfg::kSfCols;
+            const uint32_t sfb_tmem = sfa_tmem + 4 * Cfg::kKAtoms + sfb_shift;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t adesc = desc_kmajor_sw128(a_base + kk * 32);
+              const uint64_t bdesc = Cfg::kBPre ? desc_kmajor_interleave(b_base + kk * 2 * (Cfg::kHalfB * 16), Cfg::kHalfB * 16)
+                                                : desc_kmajor_sw128(b_base + kk * 32);
+              const uint32_t acc = (kb + i > w.kb0 || kk > 0);
+              if (kMode == kModeMX)
+                mma_mxf8f6f4_pair(d_tmem, adesc, bdesc, idesc_mxf8f6f4(256, kBN, kk, kk), sfa_tmem, sfb_tmem, acc);
+              else if (kMode == kModeMX4)  // K-atom kk / 2, byte pair 2 * (kk % 2)
+                mma_mxf4_pair(d_tmem, adesc, bdesc, idesc_mxf4(256, kBN, (kk & 1) * 2, (kk & 1) * 2),
+                              sfa_tmem + 4 * (kk >> 1), sfb_tmem + 4 * Cfg::kSfbAtoms * (kk >> 1), acc);
+              else
+                mma_f8f6f4_pair(d_tmem, adesc, bdesc, idesc_f8f6f4(256, kBN), acc);
+            }
+            tc_commit_pair_mc(&empty[s], kBoth);
+            if (++s == ST) { s = 0; ph ^= 1; }
           }
-          tc_commit_pair_mc(&empty[s], kBoth);
-          if (++s == ST) { s = 0; ph ^= 1; }
+          if (ok && mode_mx(kMode)) tc_commit_pair(&grp_done[slot]);  // the group's TMEM scale sets are free again
         }
         if (!ok) break;
         tc_commit_pair_mc(&acc_full[as], kBoth);
@@ -245,47 +267,96 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     }
     __syncwarp();
   } else if (mode_mx(kMode) && warp == Cfg::kSfWarp) {
-    // ------------------------------------------------------------ scale copies (leader only, MX kinds)
-    // Block k's scale atoms go to set k % kSfSets once its stage has landed and
-    // the MMAs of block k - kSfSets (the set's previous reader) have retired --
-    // their commit to `empty` of that block's stage says so.  The empty phase
-    // cannot have moved on further: the MMAs of block k - kSfSets + ST wait for
-    // copies this thread has not issued yet.  Waits poll (mbar_wait_spin) so
-    // that copies of several blocks can be in flight at once.
-    if (leader && lane == 0) {
-      int s = 0;
-      uint32_t ph = 0, kblk = 0;
+    // ------------------------------------------------------------ scale atoms (MX kinds)
+    // Loader (both CTAs): group g of this pair's blocks (kSfGroup consecutive
+    // 128-K blocks of one unit) comes in as one SFA and one SFB box into slot
+    // g % 2, counted on the leader's sf_full; the slot is refilled once the
+    // leader's copies of group g - 2 retired (sf_empty, multicast to both CTAs).
+    // Copier (leader): once group g has landed and the MMAs of group g - 2 (the
+    // previous readers of its TMEM sets) retired, tcgen05.cp of both CTAs' atoms
+    // into sets (g % 2) * kSfGroup + i, then commits to grp_full and sf_empty.
+    // The loader stays one group ahead of the copier.  Barrier phases cannot
+    // run two ahead of a waiter: each refill waits on the use it replaces.
+    // Waits poll (mbar_wait_spin) in the thread that issues tcgen05.cp.
+    if (lane == 0) {
+      constexpr int G = Cfg::kSfGroup;
+      constexpr uint16_t kBoth = 0x3;
+      int lu = pair, lkb = 0;
+      Unit lw{};
+      bool lvalid = lu < p.num_units;
+      if (lvalid) { lw = decode_unit(lu, p); lkb = lw.kb0; }
+      uint32_t gl = 0, gc = 0;  // groups loaded / copied
       bool ok = true;
-      for (int u = pair; u < p.num_units && ok; u += pp.num_pairs) {
-        const Unit w = decode_unit(u, p);
-        for (int kb = w.kb0; kb < w.kb1; ++kb, ++kblk) {
-          if (!mbar_wait_spin(&full[s], ph, abort_flag, p.status, kDevTimeoutMma, tmo)) { ok = false; break; }
-          if (kblk >= static_cast<uint32_t>(Cfg::kSfSets)) {
-            const uint32_t j = kblk - Cfg::kSfSets;
-            if (!mbar_wait_spin(&empty[j % ST], (j / ST) & 1u, abort_flag, p.status, kDevTimeoutMma, tmo)) {
+      auto load_next = [&]() -> bool {
+        if (!lvalid) return true;
+        const uint32_t slot = gl & 1u;
+        if (gl >= 2 && !mbar_wait_spin(&sf_empty[slot], ((gl - 2) >> 1) & 1u, abort_flag, p.status, kDevTimeoutProducer, tmo))
+          return false;
+        const uint32_t bar = mapa_shared(smem_u32(&sf_full[slot]), 0);
+        if (leader) mbar_arrive_expect_tx(&sf_full[slot], Cfg::kSfTxPerSlot);
+        uint8_t* dst = smem + Cfg::kOffSf + slot * Cfg::kSfSlotBytes;
+        const int ka = lkb * Cfg::kKAtoms;
+        // (128 words, K-atoms, row blocks) boxes of the atom-layout buffers,
+        // landing as [K-atom][512 B] and [row block][K-atom][512 B]
+        tma_load_4d_pair(dst, &tm_sfa, bar, 0, ka, lw.mt * 2 + static_cast<int>(rank), lw.b);
+        tma_load_4d_pair(dst + Cfg::kSfaSlotBytes, &tm_sfb, bar, 0, ka, (lw.nt * kBN) >> 7, lw.b);
+        ++gl;
+        lkb += G;
+        if (lkb >= lw.kb1) {
+          lu += pp.num_pairs;
+          lvalid = lu < p.num_units;
+          if (lvalid) { lw = decode_unit(lu, p); lkb = lw.kb0; }
+        }
+        return true;
+      };
+      if (leader) {
+        tma_prefetch_desc(&tm_sfa);
+        tma_prefetch_desc(&tm_sfb);
+        ok = load_next();
+        for (int u = pair; u < p.num_units && ok; u += pp.num_pairs) {
+          const Unit w = decode_unit(u, p);
+          for (int kb = w.kb0; kb < w.kb1; kb += G, ++gc) {
+            if (!load_next()) { ok = false; break; }
+            const int gs = min(G, w.kb1 - kb);
+            const uint32_t slot = gc & 1u;
+            if (!mbar_wait_spin(&sf_full[slot], (gc >> 1) & 1u, abort_flag, p.status, kDevTimeoutMma, tmo)) { ok = false; break; }
+            if (gc >= 2 && !mbar_wait_spin(&grp_done[slot], ((gc - 2) >> 1) & 1u, abort_flag, p.status, kDevTimeoutMma, tmo)) {
               ok = false;
               break;
             }
-          }
-          tc_fence_after();
-          const uint32_t set_col = tmem_base + Cfg::kSfCol0 + (kblk % Cfg::kSfSets) * Cfg::kSfCols;
+            tc_fence_after();
+            const uint8_t* src = smem + Cfg::kOffSf + slot * Cfg::kSfSlotBytes;
 #pragma unroll
-          for (int q = 0; q < Cfg::kKAtoms; ++q) {
-            tc_cp_32x128b_warpx4_pair(set_col + 4 * q,
-                                      desc_sf_atom(smem_u32(smem + Cfg::kOffSfa + s * Cfg::kSfaBytes + q * 512)));
+            for (int i = 0; i < G; ++i) {
+              if (i >= gs) break;
+              const uint32_t set_col = tmem_base + Cfg::kSfCol0 + (slot * G + i) * Cfg::kSfCols;
 #pragma unroll
-            for (int j = 0; j < Cfg::kSfbAtoms; ++j)
-              tc_cp_32x128b_warpx4_pair(set_col + 4 * Cfg::kKAtoms + 4 * (q * Cfg::kSfbAtoms + j),
-                                        desc_sf_atom(smem_u32(smem + Cfg::kOffSfb + s * Cfg::kSfbBytes +
-                                                              (j * Cfg::kKAtoms + q) * 512)));
+              for (int q = 0; q < Cfg::kKAtoms; ++q) {
+                tc_cp_32x128b_warpx4_pair(set_col + 4 * q, desc_sf_atom(smem_u32(src + (i * Cfg::kKAtoms + q) * 512)));
+#pragma unroll
+                for (int j = 0; j < Cfg::kSfbAtoms; ++j)
+                  tc_cp_32x128b_warpx4_pair(
+                      set_col + 4 * Cfg::kKAtoms + 4 * (q * Cfg::kSfbAtoms + j),
+                      desc_sf_atom(smem_u32(src + Cfg::kSfaSlotBytes + ((j * G + i) * Cfg::kKAtoms + q) * 512)));
+              }
+            }
+            tc_commit_pair(&grp_full[slot]);
+            tc_commit_pair_mc(&sf_empty[slot], kBoth);
           }
-          tc_commit_pair(&sf_full[kblk % Cfg::kSfSets]);
-          if (++s == ST) { s = 0; ph ^= 1; }
+        }
+        tc_commit_pair(sf_fin);  // every copy retired before TMEM is freed
+        volatile int no_abort = 0;
+        mbar_wait(sf_fin, 0, &no_abort, p.status, kDevTimeoutDrain, 1000000000ull);
+        if (*abort_flag)  // boxes still in flight land before the CTA exits
+          for (uint32_t g2 = gc; g2 < gl; ++g2)
+            mbar_wait(&sf_full[g2 & 1u], (g2 >> 1) & 1u, &no_abort, p.status, kDevTimeoutDrain, 100000000ull);
+      } else {
+        while (ok && lvalid) ok = load_next();
+        if (*abort_flag) {  // boxes signal the leader; give any in flight time to land
+          const uint64_t t0 = globaltimer_ns();
+          while (globaltimer_ns() - t0 < 2000000ull) sleep_ns(10000);
         }
       }
-      tc_commit_pair(sf_fin);  // every copy retired before TMEM is freed
-      volatile int no_abort = 0;
-      mbar_wait(sf_fin, 0, &no_abort, p.status, kDevTimeoutDrain, 1000000000ull);
     }
     __syncwarp();
   } else {
