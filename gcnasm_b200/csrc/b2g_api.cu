@@ -1002,8 +1002,8 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
   }
 
   if (pair) {
-    // scale atoms as (128 words, K-atom, row block, batch) boxes of kPairSfGroup
-    // 128-K blocks (one box per operand brings a group of blocks' atoms)
+    // scale atoms as (128 words, K-atom, row block, batch) boxes of
+    // pair_sf_group(mode) 128-K blocks (one box per operand brings a group's atoms)
     CUtensorMap tsa, tsb;
     memset(&tsa, 0, sizeof(tsa));
     memset(&tsb, 0, sizeof(tsb));
@@ -1016,7 +1016,7 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
         const long long bstr = which ? r.sfb_bstride : r.sfa_bstride;
         cuuint64_t dims[4] = {128, (cuuint64_t)kb4, (cuuint64_t)rb, (cuuint64_t)r.batch};
         cuuint64_t str[3] = {512, (cuuint64_t)(kb4 * 512), (cuuint64_t)(r.batch > 1 ? bstr : rb * kb4 * 512)};
-        cuuint32_t box[4] = {128, (cuuint32_t)(ka * kPairSfGroup), (cuuint32_t)(which ? 2 : 1), 1};
+        cuuint32_t box[4] = {128, (cuuint32_t)(ka * pair_sf_group(r.mode)), (cuuint32_t)(which ? 2 : 1), 1};
         rc = encode(which ? &tsb : &tsa, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, which ? (const void*)r.sfb : (const void*)r.sfa,
                     dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
         if (rc) return rc;

@@ -37,7 +37,9 @@ namespace b2g {
 
 // 128-K blocks whose scale atoms one TMA box brings in (the pair kernel's MX kinds);
 // the host encodes the scale tensor maps with boxes of this many blocks.
-constexpr int kPairSfGroup = 4;
+// Four for both MX kinds (MXFP4 with groups of two and a sixth operand stage ran
+// 4280-4497 instead of 5088-5194 TFLOP/s at 8192^3).
+__host__ __device__ constexpr int pair_sf_group(int /*mode*/) { return 4; }
 
 template <int kMode_, int kBN_, bool kBPre_, bool kOutF32_, bool kEpi_ = false>
 struct PairCfg {
@@ -56,7 +58,7 @@ struct PairCfg {
   static constexpr int kABytes = kHalf * 128;
   static constexpr int kBBytes = kHalfB * 128;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = 6 - (kMode == kModeMX4 ? 1 : 0);  // MXFP4's larger scale slots leave room for 5
+  static constexpr int kStages = (kMode == kModeMX4 && pair_sf_group(kMode) > 2) ? 5 : 6;  // room left by the scale slots
   static constexpr uint32_t kTxPerStage = 2u * kStageBytes;      // both CTAs complete on the leader's barrier
 
   // Scale atoms travel apart from the operand stages: one TMA box per operand
@@ -69,7 +71,7 @@ struct PairCfg {
   // columns (the even shift CUTLASS's N=192 tiles use).
   static constexpr int kSfbAtoms = 2;
   static constexpr int kKAtoms = mode_atoms(kMode);  // scale K-atoms per 128-byte K block
-  static constexpr int kSfGroup = mode_mx(kMode) ? kPairSfGroup : 1;
+  static constexpr int kSfGroup = mode_mx(kMode) ? pair_sf_group(kMode) : 1;
   static constexpr int kSfaSlotBytes = 512 * kKAtoms * kSfGroup;  // [K-atom][512 B]
   static constexpr int kSfbSlotBytes = 512 * kSfbAtoms * kKAtoms * kSfGroup;  // [row block][K-atom][512 B]
   static constexpr int kSfSlotBytes = kSfaSlotBytes + kSfbSlotBytes;
@@ -222,8 +224,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         const uint32_t d_tmem = tmem_base + as * kBN;
         // B scales of tile row 0 sit ((nt * BN) % 128) / 32 TMEM columns into the first atom
         const uint32_t sfb_shift = ((w.nt * kBN) & 127) >> 5;
-        for (int kb = w.kb0; kb < w.kb1 && ok; kb += G, ++g) {
-          const int gs = min(G, w.kb1 - kb);
+        for (int kb = w.kb0; kb < w.kb1; kb += G, ++g) {
+          const int gs = G == 1 ? 1 : min(G, w.kb1 - kb);
           const uint32_t slot = g & 1u;
           if (mode_mx(kMode) && !mbar_wait(&grp_full[slot], (g >> 1) & 1u, abort_flag, p.status, kDevTimeoutMma, tmo)) {
             ok = false;
@@ -255,7 +257,8 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             tc_commit_pair_mc(&empty[s], kBoth);
             if (++s == ST) { s = 0; ph ^= 1; }
           }
-          if (ok && mode_mx(kMode)) tc_commit_pair(&grp_done[slot]);  // the group's TMEM scale sets are free again
+          if (!ok) break;
+          if (mode_mx(kMode)) tc_commit_pair(&grp_done[slot]);  // the group's TMEM scale sets are free again
         }
         if (!ok) break;
         tc_commit_pair_mc(&acc_full[as], kBoth);
