@@ -434,7 +434,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             break;
           }
           if (kMode == kModeBlk) {
-            if (!mbar_wait(&acc_empty[as], aph ^ 1, abort_flag, p.status, kDevTimeoutMma, tmo)) { ok = false; break; }
+            // a partial buffer frees every K block: poll, the wait is short and a suspended
+            // thread wakes late (same-box A/B: 0-10 % faster over the C3 shapes)
+            if (!mbar_wait_spin(&acc_empty[as], aph ^ 1, abort_flag, p.status, kDevTimeoutMma, tmo)) { ok = false; break; }
           }
           tc_fence_after();
           const uint32_t a_base = smem_u32(smem + Cfg::kOffA + s * Cfg::kABytes);
@@ -551,7 +553,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             const float x = __shfl_sync(0xffffffffu, sa, r8 + 8 * i);
             sa2[i] = make_float2(x, x);
           }
-          if (!mbar_wait(&acc_full[as], aph, abort_flag, p.status, kDevTimeoutEpilogue, tmo)) { ok = false; break; }
+          if (!mbar_wait_spin(&acc_full[as], aph, abort_flag, p.status, kDevTimeoutEpilogue, tmo)) { ok = false; break; }
           tc_fence_after();
 #pragma unroll
           for (int c = 0; c < NC / 32; ++c) {  // 32 columns: groups j = 4c .. 4c + 3
@@ -695,7 +697,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
             if (4 * lane < NC) *reinterpret_cast<float4*>(sb_stage + 4 * lane) = sb;
             __syncwarp();
           }
-          if (!mbar_wait(&acc_full[as], aph, abort_flag, p.status, kDevTimeoutEpilogue, tmo)) { ok = false; break; }
+          if (!mbar_wait_spin(&acc_full[as], aph, abort_flag, p.status, kDevTimeoutEpilogue, tmo)) { ok = false; break; }
           tc_fence_after();
           const float s_const = sa * __shfl_sync(0xffffffffu, sb.x, 0);
           // the K block's partial in 32-column groups, one wait per group (64 columns

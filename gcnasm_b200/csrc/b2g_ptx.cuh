@@ -94,8 +94,10 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// mbar_wait for a thread that issues tcgen05.cp: it polls with the
-// non-blocking test_wait.  A blocking try_wait in a thread with scale copies in
+// mbar_wait that polls with the non-blocking test_wait.  Used by every thread
+// that issues tcgen05.cp, and for waits that are short and come every K block
+// (the blockwise kernel's partial-buffer handoffs), where a suspended thread
+// wakes late.  A blocking try_wait in a thread with scale copies in
 // flight returns only once those copies have finished, even when the phase it
 // waits for completed long before (measured on B200: 634 instead of 512 clocks
 // per 128-K block of MMAs), which holds the issuing thread to one block ahead
