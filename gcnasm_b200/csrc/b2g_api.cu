@@ -643,12 +643,35 @@ int launch_skinny(const Env& d, const CUtensorMap& tw, const CUtensorMap& ta, co
   cfg.blockDim = dim3(Cfg::kThreads);
   cfg.dynamicSmemBytes = Cfg::kSmemBytes;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = use_pdl() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  B2G_CUDA(cudaLaunchKernelEx(&cfg, b2g_gemm_skinny_kernel<Cfg>, tw, ta, sp));
+  SkinnyParams spl = sp;
+  if (spl.cluster_fold > 1) {
+    // clusters of k CTAs, only if the whole grid fits on the GPU at once (the pieces of
+    // a tile wait for one another); otherwise the L2 fold
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = spl.cluster_fold;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+    static std::atomic<int> fit_k[5] = {-1, -1, -1, -1, -1};  // clusters that fit at once, per k (queried once)
+    int fit = fit_k[spl.cluster_fold].load();
+    if (fit < 0) {
+      if (cudaOccupancyMaxActiveClusters(&fit, b2g_gemm_skinny_kernel<Cfg>, &cfg) != cudaSuccess) {
+        (void)cudaGetLastError();
+        fit = 0;
+      }
+      fit_k[spl.cluster_fold].store(fit);
+    }
+    if (fit * spl.cluster_fold < grid) {
+      spl.cluster_fold = 0;
+      cfg.numAttrs = 1;
+    }
+  }
+  B2G_CUDA(cudaLaunchKernelEx(&cfg, b2g_gemm_skinny_kernel<Cfg>, tw, ta, spl));
   return B2G_OK;
 }
 
@@ -743,6 +766,20 @@ int run_skinny(const Req& r, const Env& d) {
   sp.timeout_ns = g_timeout_ns.load();
   sp.debug_stall = g_force_stall.load();
   sp.w_early = (g_static_weights.load() && use_pdl() && r.mode != kModeBlk) ? 1 : 0;
+  // Every tile split into k equal pieces, one per CTA, k CTAs per tile (the C4 long-K
+  // shapes: 32 tiles x 4 pieces on 128 CTAs): launch in clusters of k and let the
+  // pieces meet in the rank-0 CTA's shared memory (B2G_CLUSTER_FOLD=0 turns it off).
+  {
+    static const bool off = [] {
+      const char* v = getenv("B2G_CLUSTER_FOLD");
+      return v && v[0] == '0';
+    }();
+    sp.cluster_fold = 0;
+    if (!off && r.mode != kModeBlk && mp == 16 && dp_w == 0 && sp.sk_tiles == sp.NT && grid % sp.NT == 0) {
+      const int k = grid / sp.NT;
+      if ((k == 2 || k == 4) && sp.KG % k == 0) sp.cluster_fold = k;
+    }
+  }
   sp.bsa = r.bsa;
   sp.bsb = r.bsb;
   sp.stride_sfa = r.stride_sfa;

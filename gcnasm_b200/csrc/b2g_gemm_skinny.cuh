@@ -46,7 +46,10 @@ struct SkinnyCfg {
   static constexpr int kSfBytes = 512 * kKB * kKAtoms;      // per operand per stage
   static constexpr int kStageBytes = kWBytes + kABytes + 2 * kSfBytes;
   static constexpr int kMaxStages = kKB == 1 ? 8 : 5;
-  static constexpr int kStages = 225000 / kStageBytes < kMaxStages ? 225000 / kStageBytes : kMaxStages;
+  // MP = 16: room for the cluster fold buffer (three other pieces of a tile, fp32)
+  static constexpr int kFoldBytes = kMP == 16 ? 3 * kMP * 128 * 4 : 0;
+  static constexpr int kStages = (225000 - kFoldBytes) / kStageBytes < kMaxStages ? (225000 - kFoldBytes) / kStageBytes
+                                                                                  : kMaxStages;
   static constexpr int kAccStages = 2;
   static constexpr int kAccStride = kMP < 32 ? 32 : kMP;  // accumulator stages start 32-column aligned
   static constexpr int kSfCols = 8 * kKAtoms;  // weight K-atoms (4 columns each), then activation K-atoms
@@ -59,8 +62,9 @@ struct SkinnyCfg {
   static constexpr int kOffA = kOffW + kStages * kWBytes;
   static constexpr int kOffSfw = kOffA + kStages * kABytes;
   static constexpr int kOffSfa = kOffSfw + kStages * kSfBytes;
-  static constexpr int kOffBar = (kOffSfa + kStages * kSfBytes + 7) / 8 * 8;
-  static constexpr int kNumBars = 2 * kStages + 2 * kAccStages + 2;
+  static constexpr int kOffFold = (kOffSfa + kStages * kSfBytes + 15) / 16 * 16;
+  static constexpr int kOffBar = (kOffFold + kFoldBytes + 7) / 8 * 8;
+  static constexpr int kNumBars = 2 * kStages + 2 * kAccStages + 3;
   static constexpr int kOffCtl = kOffBar + kNumBars * 8;
   static constexpr int kSmemBytes = kOffCtl + 16 + 1024;
   static_assert(kStages >= 3, "ring depth");
@@ -99,6 +103,10 @@ struct SkinnyParams {
   int debug_stall;
   int w_early;  // read B and its scales before the preceding kernel completes (static weights)
   EpiTerms epi;  // beta * C and bias (C and the bias in the output type)
+  // k > 1: launched in clusters of k CTAs whose k pieces make one tile each
+  // (CTA rank j = piece j); the pieces meet in the rank-0 CTA's shared memory
+  // instead of L2 slots and counters (MP = 16, k <= 4)
+  int cluster_fold;
 };
 
 // CTA owning unit u when U units are split evenly over G CTAs (the largest c
@@ -171,6 +179,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
   uint64_t* acc_empty = bars + 2 * ST + AS;
   uint64_t* fin = bars + 2 * ST + 2 * AS;
   uint64_t* never = fin + 1;
+  uint64_t* fold_bar = never + 1;  // cluster fold: the other pieces are in (rank-0 CTA)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + Cfg::kOffCtl);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Cfg::kOffCtl + 4);
   volatile uint32_t* last_flag = reinterpret_cast<volatile uint32_t*>(smem + Cfg::kOffCtl + 8);
@@ -240,6 +249,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     for (int s = 0; s < AS; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], 4); }
     mbar_init(fin, 1);
     mbar_init(never, 1);
+    mbar_init(fold_bar, p.cluster_fold > 1 ? 4 * (p.cluster_fold - 1) : 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tm_w);
@@ -258,6 +268,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
   if (warp == 1) tmem_alloc<Cfg::kTmemCols>(tmem_holder);
   tc_fence_before();
   __syncthreads();
+  if (p.cluster_fold > 1) cluster_sync_all();  // every CTA's fold barrier is initialised before a remote arrival
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   griddep_wait();
@@ -447,9 +458,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       // This CTA's last piece of a split tile usually finishes after the tile's
       // other pieces: bring their slots into L2 while its MMAs run, and if they
       // are all in already, fold the ones after it into registers now.
+      const bool cfold = p.cluster_fold > 1 && p.cluster_fold == nseg;
       bool last = false, have_suffix = false;
       float suffix[CH];
-      if (nseg > 1 && fin_seg) {
+      if (nseg > 1 && fin_seg && !cfold) {
         if (et < nseg && et != j) bulk_prefetch_l2(piece(et) - r, MP * 128 * 4);
         if (et == 0) *last_flag = ld_acquire_gpu_u64(cnt) == all_others ? 1u : 0u;
         skinny_epi_bar();
@@ -495,6 +507,45 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
 #pragma unroll
           for (int i = 0; i < CH; ++i) x[i] = __uint_as_float(v[i]);
           store_out(mc, x);
+        }
+      } else if (cfold) {
+        // The tile's pieces are the cluster's CTAs (rank j = piece j).  Ranks > 0 write
+        // their piece into the rank-0 CTA's fold buffer (piece jj at (jj - 1) * MP * 128
+        // floats, rows as in the L2 slots) and arrive on its fold barrier; rank 0 adds
+        // them as p_0 + (p_1 + (... + p_{k-1})), the order of the L2 path, and stores C.
+        float* fbuf = reinterpret_cast<float*>(smem + Cfg::kOffFold);
+        if (j > 0) {
+          const uint32_t dst = mapa_shared(smem_u32(fbuf + (j - 1) * MP * 128 + r), 0);
+#pragma unroll 1
+          for (int mc = 0; mc < MP; mc += CH) {
+            uint32_t v[CH];
+            load_chunk(mc, v);
+#pragma unroll
+            for (int i = 0; i < CH; ++i) st_shared_cluster_f32(dst + (mc + i) * 128 * 4, __uint_as_float(v[i]));
+          }
+          fence_acq_rel_cluster();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(fold_bar), 0));
+        } else {
+          const bool in = mbar_wait_cluster(fold_bar, 0, abort_flag, p.status, kDevTimeoutEpilogue, tmo);
+          if (in) {
+#pragma unroll 1
+            for (int mc = 0; mc < MP; mc += CH) {
+              float t[CH];
+#pragma unroll
+              for (int i = 0; i < CH; ++i) t[i] = fbuf[(nseg - 2) * MP * 128 + (mc + i) * 128 + r];
+#pragma unroll 1
+              for (int jj = nseg - 2; jj >= 1; --jj) {
+#pragma unroll
+                for (int i = 0; i < CH; ++i) t[i] = fbuf[(jj - 1) * MP * 128 + (mc + i) * 128 + r] + t[i];
+              }
+              uint32_t v[CH];
+              load_chunk(mc, v);
+#pragma unroll
+              for (int i = 0; i < CH; ++i) t[i] = __uint_as_float(v[i]) + t[i];
+              store_out(mc, t);
+            }
+          }
         }
       } else {
         if (fin_seg && !last) {  // look again now that this piece is done
@@ -555,6 +606,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (p.cluster_fold > 1) cluster_sync_all();  // no CTA leaves while a peer may still write its fold buffer
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc<Cfg::kTmemCols>(tmem_base);

@@ -513,6 +513,46 @@ def test_single_cta_path_when_pairs_disabled(dev):
     assert "single-cta ok" in r.stdout
 
 
+_FOLD_SCRIPT = r'''
+import sys, numpy as np, torch
+sys.path.insert(0, sys.argv[1])
+from oracle import oracle as O
+from gcnasm_b200 import ops
+dev = torch.device("cuda:0")
+outs = []
+for (M, N, K) in ((16, 4096, 14336), (1, 4096, 14336), (16, 2048, 4096)):
+    qa, sa = O.quant_mx(O.normal_rows(31, 0, M, K)); qb, sb = O.quant_mx(O.normal_rows(32, 0, N, K))
+    T = lambda x: torch.from_numpy(np.ascontiguousarray(x)).to(dev)
+    for od in (torch.float32, torch.bfloat16):
+        out = ops.mxfp8_gemm(T(qa), T(qb), T(O.sf_to_tc_layout(sa)), T(O.sf_to_tc_layout(sb)), out_dtype=od)
+        torch.cuda.synchronize()
+        assert ops.device_status() == 0
+        outs.append(out.view(torch.uint8).cpu().numpy().ravel())
+np.save(sys.argv[2], np.concatenate(outs))
+'''
+
+
+def test_decode_cluster_fold_matches_l2_fold(dev, tmp_path):
+    """Decode shapes whose every tile is split into equal pieces, one per CTA
+    (16 x 4096 x 14336: 32 tiles x 4 pieces on 128 CTAs), run in clusters whose
+    pieces meet in shared memory; with B2G_CLUSTER_FOLD=0 they meet through L2
+    slots and counters.  Both add the pieces in the same order, so C is bit for bit
+    the same (fp32 and bf16)."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    res = {}
+    for mode in ("1", "0"):
+        f = str(tmp_path / f"fold{mode}.npy")
+        env = dict(os.environ, B2G_CLUSTER_FOLD=mode)
+        r = subprocess.run([sys.executable, "-c", _FOLD_SCRIPT, root, f], env=env, capture_output=True, text=True,
+                           timeout=600)
+        assert r.returncode == 0, r.stdout + r.stderr
+        res[mode] = np.load(f)
+    assert np.array_equal(res["1"], res["0"])
+
+
 def test_bounded_wait_pair_kernel(dev, oracle):
     """The stall hook on the CTA-pair kernel: the leader's MMA wait gives up, both
     CTAs retire through their bounded waits, and the context stays usable."""
