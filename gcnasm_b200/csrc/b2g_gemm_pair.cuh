@@ -1,13 +1,16 @@
 // b2g_gemm_pair.cuh -- CTA-pair (cluster of 2) variant of the persistent FP8 GEMM.
 //
-// Tile 256 x BN x 128 per pair (BN = 256; 192 also compiles, with a
-// double-buffered MX accumulator, but measured slower at 8192^3);
+// Tile 256 x BN x 128 per pair (BN = 256; 192 also compiles, with two MX
+// accumulator stages and seven operand stages, but measured 15 % slower at 8192^3);
 // tcgen05.mma.cta_group::2 with M = 256: CTA r of the pair holds A rows
 // [r*128, r*128 + 128) and B rows [r*BN/2, (r+1)*BN/2) of the tile in its own
 // shared memory and receives the 128 x BN accumulator of its A rows in its own
 // TMEM.  At BN = 256 that is 32 KB of operands per SM and 128-K block for
 // 128 x 256 x 128 MACs, two thirds of the 48 KB the single-CTA 128 x 256 tile
-// needs, which lets the ring hold 6 stages.
+// needs, which lets the ring hold 6 stages (5 for MXFP4 beside its scale slots).
+//
+// Warps: 0 TMA producer, 1 MMA issuer (TMEM allocation), 2-9 epilogue (two
+// column halves x four TMEM lane quarters), 10 scale warp (MX kinds only).
 //
 // Protocol (leader = cluster rank 0):
 //   * both CTAs allocate TMEM with cta_group::2 and free it after a cluster sync;
