@@ -391,7 +391,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
       tc_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[as]), 0));
+      if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&acc_empty[as]), 0));
       if (++as == AS) { as = 0; aph ^= 1; }
       float acc[NC];
 #pragma unroll

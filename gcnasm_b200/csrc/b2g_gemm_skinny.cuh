@@ -249,7 +249,9 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     for (int s = 0; s < AS; ++s) { mbar_init(&acc_full[s], 1); mbar_init(&acc_empty[s], 4); }
     mbar_init(fin, 1);
     mbar_init(never, 1);
-    mbar_init(fold_bar, p.cluster_fold > 1 ? 4 * (p.cluster_fold - 1) : 1);
+    mbar_init(fold_bar, 1);
+    // cluster fold: the other k - 1 pieces arrive as bulk copies into this CTA's fold buffer
+    if (p.cluster_fold > 1) mbar_arrive_expect_tx(fold_bar, (p.cluster_fold - 1) * MP * 128 * 4);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tm_w);
@@ -509,35 +511,39 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
           store_out(mc, x);
         }
       } else if (cfold) {
-        // The tile's pieces are the cluster's CTAs (rank j = piece j).  Ranks > 0 write
-        // their piece into the rank-0 CTA's fold buffer (piece jj at (jj - 1) * MP * 128
-        // floats, rows as in the L2 slots) and arrive on its fold barrier; rank 0 adds
-        // them as p_0 + (p_1 + (... + p_{k-1})), the order of the L2 path, and stores C.
+        // The tile's pieces are the cluster's CTAs (rank j = piece j).  Ranks > 0 stage
+        // their piece in their own fold buffer, row r's MP sums contiguous, and each
+        // warp bulk-copies its 32 rows into the rank-0 CTA's buffer (piece jj at
+        // (jj - 1) * 128 * MP floats), completing as transaction bytes on rank 0's fold
+        // barrier; rank 0 adds them as p_0 + (p_1 + (... + p_{k-1})), the order of the
+        // L2 path, and stores C.
         float* fbuf = reinterpret_cast<float*>(smem + Cfg::kOffFold);
         if (j > 0) {
-          const uint32_t dst = mapa_shared(smem_u32(fbuf + (j - 1) * MP * 128 + r), 0);
+          float* mine = fbuf + r * MP;
 #pragma unroll 1
           for (int mc = 0; mc < MP; mc += CH) {
             uint32_t v[CH];
             load_chunk(mc, v);
 #pragma unroll
-            for (int i = 0; i < CH; ++i) st_shared_cluster_f32(dst + (mc + i) * 128 * 4, __uint_as_float(v[i]));
+            for (int i = 0; i < CH; ++i) mine[mc + i] = __uint_as_float(v[i]);
           }
-          fence_acq_rel_cluster();
+          fence_proxy_async_smem();  // the generic-proxy writes above, visible to the bulk copy
           __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(fold_bar), 0));
+          if (lane == 0)
+            bulk_copy_to_cluster(mapa_shared(smem_u32(fbuf + ((j - 1) * 128 + quad * 32) * MP), 0), fbuf + quad * 32 * MP,
+                                 32 * MP * 4, mapa_shared(smem_u32(fold_bar), 0));
         } else {
-          const bool in = mbar_wait_cluster(fold_bar, 0, abort_flag, p.status, kDevTimeoutEpilogue, tmo);
+          const bool in = mbar_wait(fold_bar, 0, abort_flag, p.status, kDevTimeoutEpilogue, tmo);
           if (in) {
 #pragma unroll 1
             for (int mc = 0; mc < MP; mc += CH) {
               float t[CH];
 #pragma unroll
-              for (int i = 0; i < CH; ++i) t[i] = fbuf[(nseg - 2) * MP * 128 + (mc + i) * 128 + r];
+              for (int i = 0; i < CH; ++i) t[i] = fbuf[((nseg - 2) * 128 + r) * MP + mc + i];
 #pragma unroll 1
               for (int jj = nseg - 2; jj >= 1; --jj) {
 #pragma unroll
-                for (int i = 0; i < CH; ++i) t[i] = fbuf[(jj - 1) * MP * 128 + (mc + i) * 128 + r] + t[i];
+                for (int i = 0; i < CH; ++i) t[i] = fbuf[((jj - 1) * 128 + r) * MP + mc + i] + t[i];
               }
               uint32_t v[CH];
               load_chunk(mc, v);

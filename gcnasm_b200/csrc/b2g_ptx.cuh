@@ -82,37 +82,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
-// try_wait with cluster-scope acquire: the phase's arrivals came from other CTAs
-// of the cluster, and their shared::cluster stores before the arrival are visible
-// after it.
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// mbar_wait with cluster-scope acquire (same bounds and status codes)
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                                  int* status, int code, uint64_t timeout_ns) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  while (true) {
-    if (mbar_try_wait_cluster(bar, parity)) return true;
-    if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > timeout_ns) {
-      *abort_flag = 1;
-      if (status) atomicCAS(status, 0, code);
-      return false;
-    }
-  }
-}
-
 __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -280,12 +249,7 @@ __device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned 
 
 // GPU-scope acquire-release fence (lighter than the sequentially consistent __threadfence).
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
-__device__ __forceinline__ void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
 
-// store to the shared memory of a CTA of this cluster (a shared::cluster address, mapa)
-__device__ __forceinline__ void st_shared_cluster_f32(uint32_t cluster_addr, float v) {
-  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr), "f"(v) : "memory");
-}
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -522,6 +486,25 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
 
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// Bulk copy of `bytes` (a multiple of 16) from this CTA's shared memory into another
+// CTA's of the cluster, completing as transaction bytes on the barrier at
+// `bar_cluster` in the destination CTA (both shared::cluster addresses, mapa).
+__device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst_cluster, const void* src, uint32_t bytes,
+                                                     uint32_t bar_cluster) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(dst_cluster), "r"(smem_u32(src)), "r"(bytes), "r"(bar_cluster)
+               : "memory");
+}
+
+// Arrival on a barrier in another CTA of the cluster with the default (CTA-scope)
+// release, for signals that publish no generic-memory data -- a TMEM accumulator
+// freed after tcgen05.wait::ld and tcgen05.fence::before_thread_sync.  The
+// cluster-scope release of mbar_arrive_cluster took ~1.3 us per arrival on B200,
+// which the pair kernel paid at every tile boundary.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 __device__ __forceinline__ void cluster_sync_all() {
