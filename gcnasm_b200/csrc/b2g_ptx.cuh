@@ -484,10 +484,6 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
   return r;
 }
 
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-
 // Bulk copy of `bytes` (a multiple of 16) from this CTA's shared memory into another
 // CTA's of the cluster, completing as transaction bytes on the barrier at
 // `bar_cluster` in the destination CTA (both shared::cluster addresses, mapa).
@@ -500,9 +496,9 @@ __device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst_cluster, const
 
 // Arrival on a barrier in another CTA of the cluster with the default (CTA-scope)
 // release, for signals that publish no generic-memory data -- a TMEM accumulator
-// freed after tcgen05.wait::ld and tcgen05.fence::before_thread_sync.  The
-// cluster-scope release of mbar_arrive_cluster took ~1.3 us per arrival on B200,
-// which the pair kernel paid at every tile boundary.
+// freed after tcgen05.wait::ld and tcgen05.fence::before_thread_sync.  An arrival
+// with a cluster-scope release (mbarrier.arrive.release.cluster) took ~1.3 us on
+// B200, which the pair kernel paid at every tile boundary.
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
