@@ -987,10 +987,11 @@ int run_gemm(const Req& r, const Env* fixed_env = nullptr) {
     if (p.out_mode == kOutStore && (r.ldc * es) % 16 == 0 && (bstride * es) % 16 == 0) {
       cuuint64_t dims[3] = {(cuuint64_t)r.N, (cuuint64_t)r.M, (cuuint64_t)r.batch};
       cuuint64_t str[2] = {(cuuint64_t)(r.ldc * es), (cuuint64_t)(bstride * es)};
-      // boxes of the epilogue's store chunk (GemmCfg::kStoreChunkBytes): 32 bytes of
-      // columns for the 20-warp blockwise tile (256 wide, 128 x 128 weight scales),
-      // 64 for every other kernel
-      const long long chunk = (r.mode == kModeBlk && r.group_n != 1 && !pair && bn == 256) ? 32 : 64;
+      // boxes of the epilogue's store chunk (GemmCfg / PairCfg::kStoreChunkBytes): 32 bytes
+      // of columns for the 20-warp blockwise tile (256 wide, 128 x 128 weight scales) and
+      // the MXFP4 pair kernel, 64 for every other kernel
+      const long long chunk =
+          ((r.mode == kModeBlk && r.group_n != 1 && !pair && bn == 256) || (pair && r.mode == kModeMX4)) ? 32 : 64;
       cuuint32_t box[3] = {(cuuint32_t)(chunk / es), 32, 1};
       rc = encode(&p.tm_c, r.out_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, r.c,
                   dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);

@@ -7,7 +7,7 @@
 // shared memory and receives the 128 x BN accumulator of its A rows in its own
 // TMEM.  At BN = 256 that is 32 KB of operands per SM and 128-K block for
 // 128 x 256 x 128 MACs, two thirds of the 48 KB the single-CTA 128 x 256 tile
-// needs, which lets the ring hold 6 stages (5 for MXFP4 beside its scale slots).
+// needs, which lets the ring hold 6 stages.
 //
 // Warps: 0 TMA producer, 1 MMA issuer (TMEM allocation), 2-9 epilogue (two
 // column halves x four TMEM lane quarters), 10 scale warp (MX kinds only).
@@ -61,7 +61,11 @@ struct PairCfg {
   static constexpr int kABytes = kHalf * 128;
   static constexpr int kBBytes = kHalfB * 128;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = (kMode == kModeMX4 && pair_sf_group(kMode) > 2) ? 5 : 6;  // room left by the scale slots
+  static constexpr int kStages = 6;
+  // bytes of columns per TMA-store box of C (boxes are that x 32 rows): MXFP4's 32-byte
+  // chunks (1 KB of staging per warp) leave room for the sixth operand stage beside its
+  // 24 KB of scale slots (measured 3-9 % faster than five stages and 64-byte chunks)
+  static constexpr int kStoreChunkBytes = kMode == kModeMX4 ? 32 : 64;
   static constexpr uint32_t kTxPerStage = 2u * kStageBytes;      // both CTAs complete on the leader's barrier
 
   // Scale atoms travel apart from the operand stages: one TMA box per operand
@@ -94,7 +98,7 @@ struct PairCfg {
   static constexpr int kOffB = kOffA + kStages * kABytes;
   static constexpr int kOffSf = kOffB + kStages * kBBytes;  // + slot * kSfSlotBytes: SFA atoms, then SFB atoms
   static constexpr int kOffStageC = (kOffSf + kSfSlots * kSfSlotBytes + 1023) / 1024 * 1024;  // TMA-store staging
-  static constexpr int kStageCBytes = kEpiWarps * 2048;                                        // 2 KB per warp
+  static constexpr int kStageCBytes = kEpiWarps * 32 * kStoreChunkBytes;                      // one box per warp
   static constexpr int kOffBar = (kOffStageC + kStageCBytes + 7) / 8 * 8;
   // full, empty, acc_full, acc_empty, fin, never, then sf_full, sf_empty, grp_full,
   // grp_done (two each) and sf_fin
@@ -373,7 +377,7 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
     const int row_in_tile = static_cast<int>(rank) * 128 + quad * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
     constexpr int NC = Cfg::kColsPerThread;
-    uint8_t* stage_c = smem + Cfg::kOffStageC + ew * 2048;
+    uint8_t* stage_c = smem + Cfg::kOffStageC + ew * 32 * Cfg::kStoreChunkBytes;
     int as = 0;
     uint32_t aph = 0;
     for (int u = pair; u < p.num_units; u += pp.num_pairs) {
@@ -405,8 +409,10 @@ __global__ void __launch_bounds__(Cfg::kThreads, 1)
         }
       }
       if (p.tma_store && p.out_mode == kOutStore) {
-        tma_store_rows<NC, Cfg::kOutF32>(&p.tm_c, acc, col0, w.mt * 256 + static_cast<int>(rank) * 128 + quad * 32, w.b, stage_c, lane);
-      } else if (p.out_mode == kOutPeers) {
+        tma_store_rows<NC, Cfg::kOutF32, Cfg::kStoreChunkBytes>(&p.tm_c, acc, col0,
+                                                                 w.mt * 256 + static_cast<int>(rank) * 128 + quad * 32,
+                                                                 w.b, stage_c, lane);
+      } else if (Cfg::kStoreChunkBytes == 64 && p.out_mode == kOutPeers) {  // MXFP8 only: 2 KB of staging per warp
         peer_store_warp<NC, Cfg::kOutF32>(p, acc, w.mt * 256 + static_cast<int>(rank) * 128 + quad * 32, col0,
                                           w.mt * p.NT + w.nt, stage_c, lane);
       } else if (m < p.M) {
